@@ -1,0 +1,124 @@
+/* cra.h -- C ABI of libcra, the B200 (sm_100a) implementation of Cron Root
+ * Attention's causal 3-phase sqrt(N) sparse attention.
+ *
+ * Every entry point takes raw device pointers, sizes and element strides,
+ * enqueues work on the given CUDA stream (a cudaStream_t passed as void*;
+ * NULL = legacy default stream) and returns a status code.  Nothing here
+ * allocates device memory, synchronizes the host, or aborts the process.
+ * The caller owns every buffer, including the backward workspace.
+ *
+ * Tensor layout: q, o, d_o, dq are [batch, heads, seq_len, head_dim]; k, v,
+ * dk, dv are [batch, kv_heads, seq_len, head_dim].  A tensor is described by
+ * its base pointer and `strides[3]` = element strides of (batch, head, seq);
+ * the head_dim stride must be 1.  Base pointers must be 16-byte aligned and
+ * strides multiples of 8 elements (TMA requirements).
+ * Supported: dtype CRA_F16 / CRA_BF16, head_dim 64 or 128, 1 <= top_k <= 4,
+ * heads % kv_heads == 0.
+ *
+ * The packed global-row list ("G") holds, per (batch, kv_head) and per
+ * W-block r, R = 1 + top_k rows (R = 1 without the relay): the strided key
+ * k[r*W], then the top_k relay tokens of block r.  g_k / g_v are contiguous
+ * [batch, kv_heads, cra_global_rows(), head_dim] in the input dtype; g_src is
+ * contiguous int32 [batch, kv_heads, NB, top_k] with NB = ceil(seq_len / W).
+ */
+#ifndef CRA_H_
+#define CRA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+enum cra_status {
+  CRA_OK = 0,
+  CRA_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad size, heads % kv_heads != 0 */
+  CRA_ERR_UNSUPPORTED = 2,      /* dtype / head_dim / top_k outside the supported set */
+  CRA_ERR_MISALIGNED = 3,       /* pointer or stride violates the TMA alignment rules */
+  CRA_ERR_WORKSPACE = 4,        /* backward workspace smaller than cra_bwd_workspace_bytes() */
+  CRA_ERR_CUDA = 5,             /* a CUDA runtime call or kernel launch failed */
+  CRA_ERR_DRIVER = 6            /* the driver entry point for tensor maps is unavailable */
+};
+
+enum cra_dtype { CRA_F16 = 0, CRA_BF16 = 1 };
+
+/* Device-side error codes written to `*dev_error` (when non-null).  Set only
+ * when a kernel gave up on a bounded wait; the kernel then exits cleanly. */
+enum cra_device_error { CRA_DEV_OK = 0, CRA_DEV_WAIT_TIMEOUT = 1 };
+
+/* Human-readable text for a cra_status value. */
+const char* cra_status_string(int status);
+
+/* Library version, major * 10000 + minor * 100 + patch. */
+int cra_version(void);
+
+/* W = ceil(sqrt(seq_len)): block size, stride and local window length.
+ * Replaces `SQRT_N = int(math.ceil(math.sqrt(S)))`, core.py:3479. */
+int cra_window(int64_t seq_len);
+
+/* 1 if the relay phase is used at this length (seq_len > 2048), else 0.
+ * Replaces `skip_relay = S <= RELAY_THRESHOLD`, core.py:2832,3507. */
+int cra_relay_active(int64_t seq_len);
+
+/* Rows per (batch, kv_head) of the packed global list: NB * (1 + top_k)
+ * with the relay, NB without. */
+int64_t cra_global_rows(int64_t seq_len, int use_relay, int top_k);
+
+/* Builds the packed global list G from k / v: strided rows always, and with
+ * use_relay the top_k rows of largest ||k||^2 per W-block (ties to the lower
+ * index), scaled by exp(relay_log_scale[h]) when that pointer is non-null
+ * (fp32 [kv_heads]).  g_src may be NULL when the backward is not needed.
+ * Replaces the relay launch _relay_precompute_topk[(B*H_kv, NB)](...),
+ * core.py:3516-3534 (kernel core.py:2630-2748), and the relay scale,
+ * core.py:3541-3544. */
+int cra_relay_build(const void* k, const void* v, const int64_t* k_strides, const int64_t* v_strides, int batch,
+                    int kv_heads, int seq_len, int head_dim, int dtype, int use_relay, int top_k,
+                    const float* relay_log_scale, void* g_k, void* g_v, int32_t* g_src, void* stream);
+
+/* Forward: o = softmax over (local band + visible prefix of G) and the
+ * natural-log row log-sum-exp lse (fp32, contiguous [batch, heads, seq_len]).
+ * softmax_scale is normally 1/sqrt(head_dim).
+ * Replaces the forward launch _cron_root_attn_fwd_v14_tiled[(B, H, tiles)],
+ * core.py:3591-3610 (kernel core.py:907-1158). */
+int cra_fwd(const void* q, const void* k, const void* v, const void* g_k, const void* g_v, const int64_t* q_strides,
+            const int64_t* k_strides, const int64_t* v_strides, int batch, int heads, int kv_heads, int seq_len,
+            int head_dim, int dtype, int use_relay, int top_k, float softmax_scale, void* o, const int64_t* o_strides,
+            float* lse, int* dev_error, void* stream);
+
+/* Bytes of device workspace cra_bwd needs for these sizes (256-byte aligned
+ * base required). */
+size_t cra_bwd_workspace_bytes(int batch, int heads, int kv_heads, int seq_len, int head_dim, int use_relay,
+                               int top_k);
+
+/* Backward: dq, dk, dv (input dtype) from o, d_o and the forward's lse / G.
+ * Gradients of the relay rows are summed into dk / dv at their source
+ * positions (g_src); with relay_log_scale non-null they are multiplied by
+ * exp(relay_log_scale[h]) on the way (chain rule through the scaled rows),
+ * and d_relay_log_scale (fp32 [kv_heads], overwritten) receives
+ * sum(dG_k * G_k + dG_v * G_v) over the relay rows.
+ * Deterministic: no floating-point atomics.
+ * Replaces CronRootAttentionV14Function.backward, core.py:3626-3759, with its
+ * kernels core.py:1165-1316 (dQ), 1650-1745 (local dK/dV), 1755-1889
+ * (strided dK/dV), 2381-2492 (relay dK/dV), 2767-2815 (relay scatter). */
+int cra_bwd(const void* q, const void* k, const void* v, const void* o, const void* d_o, const float* lse,
+            const void* g_k, const void* g_v, const int32_t* g_src, const int64_t* q_strides,
+            const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides, const int64_t* do_strides,
+            int batch, int heads, int kv_heads, int seq_len, int head_dim, int dtype, int use_relay, int top_k,
+            float softmax_scale, const float* relay_log_scale, void* dq, void* dk, void* dv,
+            const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
+            float* d_relay_log_scale, void* workspace, size_t workspace_bytes, int* dev_error, void* stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CRA_H_ */
