@@ -27,6 +27,7 @@ _f = ctypes.c_float
 _SIGNATURES = {
     "cra_status_string": (ctypes.c_char_p, [_i]),
     "cra_version": (_i, []),
+    "cra_last_error_message": (ctypes.c_char_p, []),
     "cra_window": (_i, [ctypes.c_int64]),
     "cra_relay_active": (_i, [ctypes.c_int64]),
     "cra_global_rows": (ctypes.c_int64, [ctypes.c_int64, _i, _i]),
@@ -69,7 +70,8 @@ def lib():
 def check(status: int, what: str) -> None:
     if status != 0:
         msg = lib().cra_status_string(status).decode()
-        raise CraError(f"{what} failed: {msg} (status {status})")
+        detail = lib().cra_last_error_message().decode()
+        raise CraError(f"{what} failed: {msg} (status {status}): {detail}")
 
 
 def strides3(t) -> ctypes.Array:

@@ -122,6 +122,22 @@ def _stream_ptr(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+def _launch_fwd(L, qc, kc, vc, gk, gv, gsrc, alpha, B, Hq, Hkv, S, Dp, cdt, use_relay, relay_top_k, scale,
+                dev, stream):
+    """relay build + forward kernel through the C ABI; returns (o, lse)."""
+    check(L.cra_relay_build(kc.data_ptr(), vc.data_ptr(), strides3(kc), strides3(vc),
+                            B, Hkv, S, Dp, _dtype_code(cdt), use_relay, relay_top_k,
+                            alpha.data_ptr() if alpha is not None else None,
+                            gk.data_ptr(), gv.data_ptr(), gsrc.data_ptr(), stream), "cra_relay_build")
+    o = torch.empty(B, Hq, S, Dp, device=dev, dtype=cdt)
+    lse = torch.empty(B, Hq, S, device=dev, dtype=torch.float32)
+    check(L.cra_fwd(qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), gk.data_ptr(), gv.data_ptr(),
+                    strides3(qc), strides3(kc), strides3(vc), B, Hq, Hkv, S, Dp, _dtype_code(cdt),
+                    use_relay, relay_top_k, ctypes.c_float(scale), o.data_ptr(), strides3(o),
+                    lse.data_ptr(), _err_word(dev).data_ptr(), stream), "cra_fwd")
+    return o, lse
+
+
 class CronRootAttentionV14Function(torch.autograd.Function):
     """Autograd Function; same forward arguments as the reference
     (core.py:3472-3476) and the same gradient tuple shape (core.py:3759)."""
@@ -161,16 +177,9 @@ class CronRootAttentionV14Function(torch.autograd.Function):
             if alpha.numel() != Hkv:
                 raise ValueError("relay_log_scale must have H_kv elements")
         stream = _stream_ptr(dev)
-        check(L.cra_relay_build(kc.data_ptr(), vc.data_ptr(), strides3(kc), strides3(vc),
-                                B, Hkv, S, Dp, _dtype_code(cdt), use_relay, relay_top_k,
-                                alpha.data_ptr() if alpha is not None else None,
-                                gk.data_ptr(), gv.data_ptr(), gsrc.data_ptr(), stream), "cra_relay_build")
-        o = torch.empty(B, Hq, S, Dp, device=dev, dtype=cdt)
-        lse = torch.empty(B, Hq, S, device=dev, dtype=torch.float32)
-        check(L.cra_fwd(qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), gk.data_ptr(), gv.data_ptr(),
-                        strides3(qc), strides3(kc), strides3(vc), B, Hq, Hkv, S, Dp, _dtype_code(cdt),
-                        use_relay, relay_top_k, ctypes.c_float(scale), o.data_ptr(), strides3(o),
-                        lse.data_ptr(), _err_word(dev).data_ptr(), stream), "cra_fwd")
+        with torch.cuda.device(dev):
+            o, lse = _launch_fwd(L, qc, kc, vc, gk, gv, gsrc, alpha, B, Hq, Hkv, S, Dp, cdt, use_relay,
+                                 relay_top_k, scale, dev, stream)
         ctx.save_for_backward(qc, kc, vc, o, lse, gk, gv, gsrc, alpha)
         ctx.meta = (B, Hq, Hkv, S, D, Dp, use_relay, relay_top_k, scale, in_dtype, cdt,
                     relay_log_scale is not None)
@@ -193,14 +202,15 @@ class CronRootAttentionV14Function(torch.autograd.Function):
         ws_bytes = L.cra_bwd_workspace_bytes(B, Hq, Hkv, S, Dp, use_relay, top_k)
         ws = torch.empty(max(ws_bytes, 1), device=dev, dtype=torch.uint8)
         stream = _stream_ptr(dev)
-        check(L.cra_bwd(qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), o.data_ptr(), doc.data_ptr(),
-                        lse.data_ptr(), gk.data_ptr(), gv.data_ptr(), gsrc.data_ptr(),
-                        strides3(qc), strides3(kc), strides3(vc), strides3(o), strides3(doc),
-                        B, Hq, Hkv, S, Dp, _dtype_code(cdt), use_relay, top_k, ctypes.c_float(scale),
-                        alpha.data_ptr() if alpha is not None else None,
-                        dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), strides3(dq), strides3(dk), strides3(dv),
-                        dalpha.data_ptr() if dalpha is not None else None,
-                        ws.data_ptr(), ws_bytes, _err_word(dev).data_ptr(), stream), "cra_bwd")
+        with torch.cuda.device(dev):
+            check(L.cra_bwd(qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), o.data_ptr(), doc.data_ptr(),
+                            lse.data_ptr(), gk.data_ptr(), gv.data_ptr(), gsrc.data_ptr(),
+                            strides3(qc), strides3(kc), strides3(vc), strides3(o), strides3(doc),
+                            B, Hq, Hkv, S, Dp, _dtype_code(cdt), use_relay, top_k, ctypes.c_float(scale),
+                            alpha.data_ptr() if alpha is not None else None,
+                            dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), strides3(dq), strides3(dk), strides3(dv),
+                            dalpha.data_ptr() if dalpha is not None else None,
+                            ws.data_ptr(), ws_bytes, _err_word(dev).data_ptr(), stream), "cra_bwd")
 
         def fin(t):
             t = t if Dp == D else t[..., :D]

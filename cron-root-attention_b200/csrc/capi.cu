@@ -7,6 +7,8 @@
 #include <cudaTypedefs.h>
 
 #include <cmath>
+#include <cstdarg>
+#include <cstdio>
 #include <cstring>
 #include <mutex>
 
@@ -27,6 +29,16 @@ namespace {
 
 constexpr int kVersion = 100;  // 0.1.0
 
+thread_local char g_last_error[512] = "";
+
+int fail(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -40,27 +52,40 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+// Makes the calling thread's current device's primary context current.  A
+// thread that has made no CUDA runtime call yet (for example a framework's
+// backward worker whose allocations were all served from a cache) has no
+// current context, and cuTensorMapEncodeTiled then fails.
+int bind_context() {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaSetDevice(dev);
+  return e == cudaSuccess ? CRA_OK : fail(CRA_ERR_CUDA, "binding the device context: %s", cudaGetErrorString(e));
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // Checks one [dim0, dim1, rows, D] tensor description.
-int check_tensor(const void* p, const int64_t* st, int dim0, int dim1) {
-  if (!p || !st) return CRA_ERR_INVALID_ARGUMENT;
-  if (!aligned16(p)) return CRA_ERR_MISALIGNED;
+int check_tensor(const char* name, const void* p, const int64_t* st, int dim0, int dim1) {
+  if (!p || !st) return fail(CRA_ERR_INVALID_ARGUMENT, "%s: null pointer or strides", name);
+  if (!aligned16(p)) return fail(CRA_ERR_MISALIGNED, "%s: base pointer not 16-byte aligned", name);
   for (int i = 0; i < 3; ++i) {
-    if (st[i] < 0) return CRA_ERR_INVALID_ARGUMENT;
+    if (st[i] < 0) return fail(CRA_ERR_INVALID_ARGUMENT, "%s: negative stride", name);
     if (st[i] % 8 != 0) {
       const int extent = i == 0 ? dim0 : (i == 1 ? dim1 : 2);
-      if (extent > 1) return CRA_ERR_MISALIGNED;  // stride of a size-1 dim is never used
+      if (extent > 1)  // stride of a size-1 dim is never used
+        return fail(CRA_ERR_MISALIGNED, "%s: stride %d (%lld) not a multiple of 8 elements", name, i,
+                    static_cast<long long>(st[i]));
     }
   }
   return CRA_OK;
 }
 
 // 4-D tensor map over [d1 (outer), d0, rows, D] with 128 x 64 boxes, 128B swizzle.
-int make_tmap(CUtensorMap* m, const void* base, bool bf16, int D, int64_t rows, int64_t d0, int64_t d1,
-              const int64_t* st) {
+int make_tmap(const char* name, CUtensorMap* m, const void* base, bool bf16, int D, int64_t rows, int64_t d0,
+              int64_t d1, const int64_t* st) {
   auto fn = encode_fn();
-  if (!fn) return CRA_ERR_DRIVER;
+  if (!fn) return fail(CRA_ERR_DRIVER, "cuTensorMapEncodeTiled not available from the driver");
   cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(d0),
                         static_cast<cuuint64_t>(d1)};
   // byte strides of dims 1..3; a size-1 dim gets a harmless valid stride
@@ -75,20 +100,71 @@ int make_tmap(CUtensorMap* m, const void* base, bool bf16, int D, int64_t rows, 
   CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? CRA_OK : CRA_ERR_INVALID_ARGUMENT;
+  if (r != CUDA_SUCCESS)
+    return fail(CRA_ERR_INVALID_ARGUMENT,
+                "%s: cuTensorMapEncodeTiled failed (CUresult %d), dims [%llu %llu %llu %llu], byte strides "
+                "[%llu %llu %llu]",
+                name, static_cast<int>(r), (unsigned long long)dims[0], (unsigned long long)dims[1],
+                (unsigned long long)dims[2], (unsigned long long)dims[3], (unsigned long long)strides[0],
+                (unsigned long long)strides[1], (unsigned long long)strides[2]);
+  return CRA_OK;
 }
 
 int check_common(int batch, int heads, int kv_heads, int seq_len, int head_dim, int dtype, int top_k) {
-  if (batch < 1 || heads < 1 || kv_heads < 1 || seq_len < 1) return CRA_ERR_INVALID_ARGUMENT;
-  if (heads % kv_heads != 0) return CRA_ERR_INVALID_ARGUMENT;
-  if (batch > 65535 || heads > 65535) return CRA_ERR_INVALID_ARGUMENT;
-  if (dtype != CRA_F16 && dtype != CRA_BF16) return CRA_ERR_UNSUPPORTED;
-  if (head_dim != 64 && head_dim != 128) return CRA_ERR_UNSUPPORTED;
-  if (top_k < 1 || top_k > 4) return CRA_ERR_UNSUPPORTED;
+  if (batch < 1 || heads < 1 || kv_heads < 1 || seq_len < 1)
+    return fail(CRA_ERR_INVALID_ARGUMENT, "sizes must be >= 1 (batch %d heads %d kv_heads %d seq_len %d)", batch,
+                heads, kv_heads, seq_len);
+  if (heads % kv_heads != 0)
+    return fail(CRA_ERR_INVALID_ARGUMENT, "heads (%d) not a multiple of kv_heads (%d)", heads, kv_heads);
+  if (batch > 65535 || heads > 65535) return fail(CRA_ERR_INVALID_ARGUMENT, "batch or heads > 65535");
+  if (dtype != CRA_F16 && dtype != CRA_BF16) return fail(CRA_ERR_UNSUPPORTED, "dtype %d unsupported", dtype);
+  if (head_dim != 64 && head_dim != 128) return fail(CRA_ERR_UNSUPPORTED, "head_dim %d unsupported", head_dim);
+  if (top_k < 1 || top_k > 4) return fail(CRA_ERR_UNSUPPORTED, "top_k %d outside 1..4", top_k);
   return CRA_OK;
 }
 
 int rows_per_block(int use_relay, int top_k) { return use_relay ? 1 + top_k : 1; }
+
+// Backward workspace layout (all fp32, each region 256-byte aligned):
+//   lse2, delta  [B, H, Spad]              Spad = 128 * ceil(S / 128)
+//   dgk, dgv     [B, Hkv, NG, D]           reduced global-row gradients
+//   part_k/v     [n_split, B, Hkv, NG, D]  per-split partials
+struct BwdLayout {
+  int n_split;
+  size_t off_lse2, off_delta, off_dgk, off_dgv, off_pk, off_pv, total;
+};
+
+size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Query splits per 128-row global tile: enough CTAs to cover the GPU about
+// twice; a pure function of the sizes so the workspace size is predictable.
+int global_splits(int batch, int kv_heads, int seq_len, int NG) {
+  const int n_gtiles = (NG + kTile - 1) / kTile;
+  const int n_qtiles = (seq_len + kTile - 1) / kTile;
+  const long long base = static_cast<long long>(batch) * kv_heads * n_gtiles;
+  long long s = (296 + base - 1) / base;
+  if (s > 32) s = 32;
+  if (s > n_qtiles) s = n_qtiles;
+  if (s < 1) s = 1;
+  return static_cast<int>(s);
+}
+
+BwdLayout bwd_layout(int batch, int heads, int kv_heads, int seq_len, int head_dim, int use_relay, int top_k) {
+  BwdLayout L;
+  const int64_t NG = cra_global_rows(seq_len, use_relay, top_k);
+  const int64_t Spad = static_cast<int64_t>((seq_len + kTile - 1) / kTile) * kTile;
+  L.n_split = global_splits(batch, kv_heads, seq_len, static_cast<int>(NG));
+  const size_t rowsz = round256(sizeof(float) * batch * heads * Spad);
+  const size_t gsz = round256(sizeof(float) * batch * kv_heads * NG * head_dim);
+  L.off_lse2 = 0;
+  L.off_delta = L.off_lse2 + rowsz;
+  L.off_dgk = L.off_delta + rowsz;
+  L.off_dgv = L.off_dgk + gsz;
+  L.off_pk = L.off_dgv + gsz;
+  L.off_pv = L.off_pk + gsz * L.n_split;
+  L.total = L.off_pv + gsz * L.n_split;
+  return L;
+}
 
 #define CRA_TRY(x)                \
   do {                            \
@@ -115,6 +191,8 @@ const char* cra_status_string(int status) {
 
 int cra_version(void) { return kVersion; }
 
+const char* cra_last_error_message(void) { return g_last_error; }
+
 int cra_window(int64_t seq_len) {
   if (seq_len < 1) return 0;
   int w = static_cast<int>(std::ceil(std::sqrt(static_cast<double>(seq_len))));
@@ -137,30 +215,32 @@ int cra_relay_build(const void* k, const void* v, const int64_t* k_strides, cons
                     int kv_heads, int seq_len, int head_dim, int dtype, int use_relay, int top_k,
                     const float* relay_log_scale, void* g_k, void* g_v, int32_t* g_src, void* stream) {
   CRA_TRY(check_common(batch, kv_heads, kv_heads, seq_len, head_dim, dtype, top_k));
-  CRA_TRY(check_tensor(k, k_strides, batch, kv_heads));
-  CRA_TRY(check_tensor(v, v_strides, batch, kv_heads));
-  if (!g_k || !g_v) return CRA_ERR_INVALID_ARGUMENT;
-  if (!aligned16(g_k) || !aligned16(g_v)) return CRA_ERR_MISALIGNED;
+  CRA_TRY(check_tensor("k", k, k_strides, batch, kv_heads));
+  CRA_TRY(check_tensor("v", v, v_strides, batch, kv_heads));
+  if (!g_k || !g_v) return fail(CRA_ERR_INVALID_ARGUMENT, "g_k / g_v: null pointer");
+  if (!aligned16(g_k) || !aligned16(g_v)) return fail(CRA_ERR_MISALIGNED, "g_k / g_v: not 16-byte aligned");
   const int W = cra_window(seq_len);
   const int R = rows_per_block(use_relay, top_k);
   cudaError_t e = launch_relay_build(head_dim, dtype == CRA_BF16, k, v, k_strides, v_strides, batch, kv_heads,
                                      seq_len, W, top_k, R, use_relay ? relay_log_scale : nullptr, g_k, g_v,
                                      use_relay ? g_src : nullptr, static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? CRA_OK : CRA_ERR_CUDA;
+  return e == cudaSuccess ? CRA_OK : fail(CRA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
 }
 
 int cra_fwd(const void* q, const void* k, const void* v, const void* g_k, const void* g_v, const int64_t* q_strides,
             const int64_t* k_strides, const int64_t* v_strides, int batch, int heads, int kv_heads, int seq_len,
             int head_dim, int dtype, int use_relay, int top_k, float softmax_scale, void* o, const int64_t* o_strides,
             float* lse, int* dev_error, void* stream) {
+  CRA_TRY(bind_context());
   CRA_TRY(check_common(batch, heads, kv_heads, seq_len, head_dim, dtype, top_k));
-  CRA_TRY(check_tensor(q, q_strides, batch, heads));
-  CRA_TRY(check_tensor(k, k_strides, batch, kv_heads));
-  CRA_TRY(check_tensor(v, v_strides, batch, kv_heads));
-  CRA_TRY(check_tensor(o, o_strides, batch, heads));
-  if (!g_k || !g_v || !lse) return CRA_ERR_INVALID_ARGUMENT;
-  if (!aligned16(g_k) || !aligned16(g_v)) return CRA_ERR_MISALIGNED;
-  if (!(softmax_scale > 0.f) || !std::isfinite(softmax_scale)) return CRA_ERR_INVALID_ARGUMENT;
+  CRA_TRY(check_tensor("q", q, q_strides, batch, heads));
+  CRA_TRY(check_tensor("k", k, k_strides, batch, kv_heads));
+  CRA_TRY(check_tensor("v", v, v_strides, batch, kv_heads));
+  CRA_TRY(check_tensor("o", o, o_strides, batch, heads));
+  if (!g_k || !g_v || !lse) return fail(CRA_ERR_INVALID_ARGUMENT, "g_k / g_v / lse: null pointer");
+  if (!aligned16(g_k) || !aligned16(g_v)) return fail(CRA_ERR_MISALIGNED, "g_k / g_v: not 16-byte aligned");
+  if (!(softmax_scale > 0.f) || !std::isfinite(softmax_scale))
+    return fail(CRA_ERR_INVALID_ARGUMENT, "softmax_scale must be finite and > 0");
   const bool bf16 = dtype == CRA_BF16;
   const int W = cra_window(seq_len);
   const int R = rows_per_block(use_relay, top_k);
@@ -169,11 +249,11 @@ int cra_fwd(const void* q, const void* k, const void* v, const void* g_k, const 
                            head_dim};
   QueryPassParams p;
   std::memset(&p, 0, sizeof(p));
-  CRA_TRY(make_tmap(&p.tm_q, q, bf16, head_dim, seq_len, heads, batch, q_strides));
-  CRA_TRY(make_tmap(&p.tm_k, k, bf16, head_dim, seq_len, kv_heads, batch, k_strides));
-  CRA_TRY(make_tmap(&p.tm_v, v, bf16, head_dim, seq_len, kv_heads, batch, v_strides));
-  CRA_TRY(make_tmap(&p.tm_gk, g_k, bf16, head_dim, NG, kv_heads, batch, g_st));
-  CRA_TRY(make_tmap(&p.tm_gv, g_v, bf16, head_dim, NG, kv_heads, batch, g_st));
+  CRA_TRY(make_tmap("q", &p.tm_q, q, bf16, head_dim, seq_len, heads, batch, q_strides));
+  CRA_TRY(make_tmap("k", &p.tm_k, k, bf16, head_dim, seq_len, kv_heads, batch, k_strides));
+  CRA_TRY(make_tmap("v", &p.tm_v, v, bf16, head_dim, seq_len, kv_heads, batch, v_strides));
+  CRA_TRY(make_tmap("gk", &p.tm_gk, g_k, bf16, head_dim, NG, kv_heads, batch, g_st));
+  CRA_TRY(make_tmap("gv", &p.tm_gv, g_v, bf16, head_dim, NG, kv_heads, batch, g_st));
   p.tm_do = p.tm_q;
   p.out = o;
   p.out_sb = o_strides[0];
@@ -193,7 +273,137 @@ int cra_fwd(const void* q, const void* k, const void* v, const void* g_k, const 
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   p.err = dev_error;
   cudaError_t e = launch_fwd(p, head_dim, bf16, static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? CRA_OK : CRA_ERR_CUDA;
+  return e == cudaSuccess ? CRA_OK : fail(CRA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+}
+
+
+size_t cra_bwd_workspace_bytes(int batch, int heads, int kv_heads, int seq_len, int head_dim, int use_relay,
+                               int top_k) {
+  if (check_common(batch, heads, kv_heads, seq_len, head_dim, CRA_BF16, top_k) != CRA_OK) return 0;
+  return bwd_layout(batch, heads, kv_heads, seq_len, head_dim, use_relay, top_k).total;
+}
+
+int cra_bwd(const void* q, const void* k, const void* v, const void* o, const void* d_o, const float* lse,
+            const void* g_k, const void* g_v, const int32_t* g_src, const int64_t* q_strides,
+            const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides, const int64_t* do_strides,
+            int batch, int heads, int kv_heads, int seq_len, int head_dim, int dtype, int use_relay, int top_k,
+            float softmax_scale, const float* relay_log_scale, void* dq, void* dk, void* dv,
+            const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
+            float* d_relay_log_scale, void* workspace, size_t workspace_bytes, int* dev_error, void* stream) {
+  CRA_TRY(bind_context());
+  CRA_TRY(check_common(batch, heads, kv_heads, seq_len, head_dim, dtype, top_k));
+  CRA_TRY(check_tensor("q", q, q_strides, batch, heads));
+  CRA_TRY(check_tensor("k", k, k_strides, batch, kv_heads));
+  CRA_TRY(check_tensor("v", v, v_strides, batch, kv_heads));
+  CRA_TRY(check_tensor("o", o, o_strides, batch, heads));
+  CRA_TRY(check_tensor("d_o", d_o, do_strides, batch, heads));
+  CRA_TRY(check_tensor("dq", dq, dq_strides, batch, heads));
+  CRA_TRY(check_tensor("dk", dk, dk_strides, batch, kv_heads));
+  CRA_TRY(check_tensor("dv", dv, dv_strides, batch, kv_heads));
+  if (!lse || !g_k || !g_v) return fail(CRA_ERR_INVALID_ARGUMENT, "lse / g_k / g_v: null pointer");
+  if (use_relay && !g_src) return fail(CRA_ERR_INVALID_ARGUMENT, "g_src: null with the relay active");
+  if (!aligned16(g_k) || !aligned16(g_v)) return fail(CRA_ERR_MISALIGNED, "g_k / g_v: not 16-byte aligned");
+  if (!(softmax_scale > 0.f) || !std::isfinite(softmax_scale))
+    return fail(CRA_ERR_INVALID_ARGUMENT, "softmax_scale must be finite and > 0");
+  const BwdLayout lay = bwd_layout(batch, heads, kv_heads, seq_len, head_dim, use_relay, top_k);
+  if (!workspace || workspace_bytes < lay.total)
+    return fail(CRA_ERR_WORKSPACE, "workspace: %zu bytes given, %zu needed", workspace_bytes, lay.total);
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return fail(CRA_ERR_MISALIGNED, "workspace: base not 256-byte aligned");
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const bool bf16 = dtype == CRA_BF16;
+  const int W = cra_window(seq_len);
+  const int R = rows_per_block(use_relay, top_k);
+  const int NG = static_cast<int>(cra_global_rows(seq_len, use_relay, top_k));
+  const int NB = (seq_len + W - 1) / W;
+  const int64_t g_st[3] = {static_cast<int64_t>(kv_heads) * NG * head_dim, static_cast<int64_t>(NG) * head_dim,
+                           head_dim};
+  BwdLaunch L;
+  std::memset(&L, 0, sizeof(L));
+  float* lse2 = reinterpret_cast<float*>(ws + lay.off_lse2);
+  float* delta = reinterpret_cast<float*>(ws + lay.off_delta);
+  QueryPassParams& qp = L.qp;
+  CRA_TRY(make_tmap("q", &qp.tm_q, q, bf16, head_dim, seq_len, heads, batch, q_strides));
+  CRA_TRY(make_tmap("k", &qp.tm_k, k, bf16, head_dim, seq_len, kv_heads, batch, k_strides));
+  CRA_TRY(make_tmap("v", &qp.tm_v, v, bf16, head_dim, seq_len, kv_heads, batch, v_strides));
+  CRA_TRY(make_tmap("g_k", &qp.tm_gk, g_k, bf16, head_dim, NG, kv_heads, batch, g_st));
+  CRA_TRY(make_tmap("g_v", &qp.tm_gv, g_v, bf16, head_dim, NG, kv_heads, batch, g_st));
+  CRA_TRY(make_tmap("d_o", &qp.tm_do, d_o, bf16, head_dim, seq_len, heads, batch, do_strides));
+  qp.out = dq;
+  qp.out_sb = dq_strides[0];
+  qp.out_sh = dq_strides[1];
+  qp.out_ss = dq_strides[2];
+  qp.lse = lse2;
+  qp.delta = delta;
+  qp.B = batch;
+  qp.H = heads;
+  qp.kv_groups = heads / kv_heads;
+  qp.S = seq_len;
+  qp.W = W;
+  qp.R = R;
+  qp.NG = NG;
+  qp.n_qtiles = (seq_len + kTile - 1) / kTile;
+  qp.scale = softmax_scale;
+  qp.scale_log2 = softmax_scale * 1.4426950408889634f;
+  qp.err = dev_error;
+  for (int mode = 0; mode < 2; ++mode) {
+    KeyPassParams& kp = mode ? L.local : L.global;
+    kp.tm_q = qp.tm_q;
+    kp.tm_do = qp.tm_do;
+    kp.tm_k = mode ? qp.tm_k : qp.tm_gk;
+    kp.tm_v = mode ? qp.tm_v : qp.tm_gv;
+    kp.lse = lse2;
+    kp.delta = delta;
+    kp.dk = dk;
+    kp.dv = dv;
+    kp.dk_sb = dk_strides[0];
+    kp.dk_sh = dk_strides[1];
+    kp.dk_ss = dk_strides[2];
+    kp.dv_sb = dv_strides[0];
+    kp.dv_sh = dv_strides[1];
+    kp.dv_ss = dv_strides[2];
+    kp.dgk = reinterpret_cast<float*>(ws + lay.off_dgk);
+    kp.dgv = reinterpret_cast<float*>(ws + lay.off_dgv);
+    kp.gsrc = g_src;
+    kp.relay_scale = use_relay ? relay_log_scale : nullptr;
+    kp.part_k = reinterpret_cast<float*>(ws + lay.off_pk);
+    kp.part_v = reinterpret_cast<float*>(ws + lay.off_pv);
+    kp.B = batch;
+    kp.H = heads;
+    kp.kv_groups = heads / kv_heads;
+    kp.S = seq_len;
+    kp.W = W;
+    kp.R = R;
+    kp.NB = NB;
+    kp.NG = NG;
+    kp.top_k = top_k;
+    kp.n_ktiles = (seq_len + kTile - 1) / kTile;
+    kp.n_split = lay.n_split;
+    kp.scale = softmax_scale;
+    kp.scale_log2 = qp.scale_log2;
+    kp.err = dev_error;
+  }
+  L.o = o;
+  L.d_o = d_o;
+  for (int i = 0; i < 3; ++i) {
+    L.o_st[i] = o_strides[i];
+    L.do_st[i] = do_strides[i];
+  }
+  L.lse_in = lse;
+  L.lse2 = lse2;
+  L.delta = delta;
+  L.dgk = reinterpret_cast<float*>(ws + lay.off_dgk);
+  L.dgv = reinterpret_cast<float*>(ws + lay.off_dgv);
+  L.d_alpha = (use_relay && relay_log_scale) ? d_relay_log_scale : nullptr;
+  L.gk_rows = g_k;
+  L.gv_rows = g_v;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (d_relay_log_scale && !L.d_alpha) {
+    const cudaError_t me = cudaMemsetAsync(d_relay_log_scale, 0, sizeof(float) * kv_heads, st);
+    if (me != cudaSuccess) return fail(CRA_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(me));
+  }
+  cudaError_t e = launch_bwd(L, head_dim, bf16, st);
+  return e == cudaSuccess ? CRA_OK : fail(CRA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
 }
 
 }  // extern "C"

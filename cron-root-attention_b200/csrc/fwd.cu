@@ -56,10 +56,6 @@ struct FwdCfg {
   static constexpr int COL_S0 = 0, COL_S1 = 128, COL_O = 256;
 };
 
-__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
-  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
-}
-
 template <int D, bool BF16>
 __global__ void __launch_bounds__(256, 1) fwd_kernel(const __grid_constant__ QueryPassParams p) {
   using C = FwdCfg<D>;

@@ -40,7 +40,7 @@ struct alignas(64) KeyPassParams {
   int64_t dk_sb, dk_sh, dk_ss, dv_sb, dv_sh, dv_ss;
   const float* dgk; const float* dgv;
   const int32_t* gsrc;     // [B, Hkv, NB, TOP_K]
-  const float* relay_scale;// [Hkv] exp(alpha) per kv head, or null
+  const float* relay_scale;// [Hkv] relay_log_scale (alpha) per kv head, or null
   // global mode: fp32 partial outputs [n_split, B, Hkv, NG, D]
   float* part_k; float* part_v;
   int B, H, kv_groups, S, W, R, NB, NG, top_k;
@@ -49,5 +49,25 @@ struct alignas(64) KeyPassParams {
   float scale, scale_log2;
   int* err;
 };
+
+// Everything one backward launch sequence needs (bwd.cu).
+struct BwdLaunch {
+  QueryPassParams qp;      // dQ pass (lse / delta point at the padded arrays)
+  KeyPassParams global;    // dG over global rows -> partials
+  KeyPassParams local;     // dK / dV over the local band (+ dG fold-in)
+  const void* o;
+  const void* d_o;
+  int64_t o_st[3], do_st[3];
+  const float* lse_in;     // forward lse [B, H, S]
+  float* lse2;             // [B, H, Spad] lse * log2(e)
+  float* delta;            // [B, H, Spad] rowsum(O * dO)
+  float* dgk;              // [B, Hkv, NG, D] reduced global-row gradients
+  float* dgv;
+  float* d_alpha;          // [Hkv] or null
+  const void* gk_rows;     // G_k / G_v (for d_alpha)
+  const void* gv_rows;
+};
+
+cudaError_t launch_bwd(const BwdLaunch& L, int D, bool bf16, cudaStream_t stream);
 
 }  // namespace cra

@@ -33,7 +33,7 @@ enum DeviceError : int {
 };
 
 #ifndef CRA_WAIT_LIMIT_NS
-#define CRA_WAIT_LIMIT_NS 2000000000ull  // 2 s: far above any legitimate wait
+#define CRA_WAIT_LIMIT_NS 500000000ull  // 0.5 s: far above any legitimate wait
 #endif
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -111,6 +111,14 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* m, 
       "[%6];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(m)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
       : "memory");
+}
+
+// Untiled bulk copy global -> shared (16-byte aligned addresses, size a
+// multiple of 16), completing `bytes` on barrier `bar`.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+               : "memory");
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -209,6 +217,17 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+// Bounded spin used only on abort paths (no abort flag to consult).
+__device__ __forceinline__ void mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try(bar, parity) && globaltimer() - t0 < CRA_WAIT_LIMIT_NS) {
+  }
 }
 
 // ---------------------------------------------------------------------------

@@ -54,6 +54,10 @@ enum cra_device_error { CRA_DEV_OK = 0, CRA_DEV_WAIT_TIMEOUT = 1 };
 /* Human-readable text for a cra_status value. */
 const char* cra_status_string(int status);
 
+/* Detail text for the last non-zero status returned on the calling thread
+ * (which tensor or size was rejected, or which CUDA call failed). */
+const char* cra_last_error_message(void);
+
 /* Library version, major * 10000 + minor * 100 + patch. */
 int cra_version(void);
 
