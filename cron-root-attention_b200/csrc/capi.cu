@@ -231,7 +231,6 @@ int cra_fwd(const void* q, const void* k, const void* v, const void* g_k, const 
             const int64_t* k_strides, const int64_t* v_strides, int batch, int heads, int kv_heads, int seq_len,
             int head_dim, int dtype, int use_relay, int top_k, float softmax_scale, void* o, const int64_t* o_strides,
             float* lse, int* dev_error, void* stream) {
-  CRA_TRY(bind_context());
   CRA_TRY(check_common(batch, heads, kv_heads, seq_len, head_dim, dtype, top_k));
   CRA_TRY(check_tensor("q", q, q_strides, batch, heads));
   CRA_TRY(check_tensor("k", k, k_strides, batch, kv_heads));
@@ -247,6 +246,7 @@ int cra_fwd(const void* q, const void* k, const void* v, const void* g_k, const 
   const int NG = static_cast<int>(cra_global_rows(seq_len, use_relay, top_k));
   const int64_t g_st[3] = {static_cast<int64_t>(kv_heads) * NG * head_dim, static_cast<int64_t>(NG) * head_dim,
                            head_dim};
+  CRA_TRY(bind_context());
   QueryPassParams p;
   std::memset(&p, 0, sizeof(p));
   CRA_TRY(make_tmap("q", &p.tm_q, q, bf16, head_dim, seq_len, heads, batch, q_strides));
@@ -290,7 +290,6 @@ int cra_bwd(const void* q, const void* k, const void* v, const void* o, const vo
             float softmax_scale, const float* relay_log_scale, void* dq, void* dk, void* dv,
             const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
             float* d_relay_log_scale, void* workspace, size_t workspace_bytes, int* dev_error, void* stream) {
-  CRA_TRY(bind_context());
   CRA_TRY(check_common(batch, heads, kv_heads, seq_len, head_dim, dtype, top_k));
   CRA_TRY(check_tensor("q", q, q_strides, batch, heads));
   CRA_TRY(check_tensor("k", k, k_strides, batch, kv_heads));
@@ -318,6 +317,7 @@ int cra_bwd(const void* q, const void* k, const void* v, const void* o, const vo
   const int NB = (seq_len + W - 1) / W;
   const int64_t g_st[3] = {static_cast<int64_t>(kv_heads) * NG * head_dim, static_cast<int64_t>(NG) * head_dim,
                            head_dim};
+  CRA_TRY(bind_context());
   BwdLaunch L;
   std::memset(&L, 0, sizeof(L));
   float* lse2 = reinterpret_cast<float*>(ws + lay.off_lse2);

@@ -127,8 +127,11 @@ def _gather_rows(x: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
 def forward(q, k, v, *, use_relay: Optional[bool] = None, top_k: int = 2,
             relay_log_scale: Optional[torch.Tensor] = None,
             relay_idx: Optional[torch.Tensor] = None, W: Optional[int] = None,
-            chunk: int = 256, dtype=torch.float32, kv_groups: int = 1):
+            chunk: int = 256, dtype=torch.float32, kv_groups: int = 1, rows=None):
     """Forward restatement of cpu_reference.py:198-339 (``cra_cpu_fast``).
+
+    ``rows=(r0, r1)`` computes only query rows [r0, r1) (others are left 0);
+    each row depends only on its own keys, so those rows are exact.
 
     Same chunked single-pass softmax: per chunk of ``chunk`` queries, scores
     against the local window and against the concatenated strided+relay rows,
@@ -158,11 +161,12 @@ def forward(q, k, v, *, use_relay: Optional[bool] = None, top_k: int = 2,
                         torch.ones((), dtype=dtype))
         Kg = Kg * f
         Vg = Vg * f
-    out = torch.empty(B, Hq, S, D, dtype=dtype)
-    lse = torch.empty(B, Hq, S, dtype=dtype)
+    out = torch.zeros(B, Hq, S, D, dtype=dtype)
+    lse = torch.zeros(B, Hq, S, dtype=dtype)
     pos = torch.arange(S)
-    for q0 in range(0, S, chunk):
-        q1 = min(q0 + chunk, S)
+    r0, r1 = rows if rows is not None else (0, S)
+    for q0 in range(r0, r1, chunk):
+        q1 = min(q0 + chunk, r1)
         qc = q[:, :, q0:q1]
         w0 = max(0, q0 - W + 1)
         Kw, Vw = k[:, :, w0:q1], v[:, :, w0:q1]
@@ -188,8 +192,11 @@ def forward(q, k, v, *, use_relay: Optional[bool] = None, top_k: int = 2,
 def forward_backward(q, k, v, do, *, use_relay: Optional[bool] = None, top_k: int = 2,
                      relay_log_scale: Optional[torch.Tensor] = None,
                      relay_idx: Optional[torch.Tensor] = None, W: Optional[int] = None,
-                     chunk: int = 256, dtype=torch.float64, kv_groups: int = 1):
+                     chunk: int = 256, dtype=torch.float64, kv_groups: int = 1, rows=None):
     """Differentiable restatement; returns (out, dq, dk, dv, d_relay_log_scale).
+
+    ``rows=(r0, r1)`` restricts the loss to query rows [r0, r1): dq of those
+    rows is then exact (dk / dv only receive those rows' contributions).
 
     Autograd through gathered relay rows sends each relay row's gradient to
     its source token (what core.py:2767-2815 does on the GPU).  The relay
@@ -227,8 +234,9 @@ def forward_backward(q, k, v, do, *, use_relay: Optional[bool] = None, top_k: in
         Vg = Vg * f
     pos = torch.arange(S)
     outs = []
-    for q0 in range(0, S, chunk):
-        q1 = min(q0 + chunk, S)
+    r0, r1 = rows if rows is not None else (0, S)
+    for q0 in range(r0, r1, chunk):
+        q1 = min(q0 + chunk, r1)
         qc = q[:, :, q0:q1]
         w0 = max(0, q0 - W + 1)
         qp = pos[q0:q1].view(-1, 1)
@@ -243,8 +251,8 @@ def forward_backward(q, k, v, do, *, use_relay: Optional[bool] = None, top_k: in
         outs.append(torch.matmul(p[..., :nl], vv[:, :, w0:q1]) + torch.matmul(p[..., nl:], Vg))
     out = torch.cat(outs, dim=2)
     grads = torch.autograd.grad(out, [q, k, v] + ([alpha] if alpha is not None else []),
-                                grad_outputs=do.to(dtype), allow_unused=True)
-    dq, dk, dv = grads[:3]
+                                grad_outputs=do.to(dtype)[:, :, r0:r1], allow_unused=True)
+    dq, dk, dv = (g if g is not None else torch.zeros_like(t) for g, t in zip(grads[:3], (q, k, v)))
     da = grads[3] if alpha is not None else None
     if da is None and alpha is not None:
         da = torch.zeros_like(alpha)

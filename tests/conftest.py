@@ -12,7 +12,6 @@ for p in (ROOT, PKG):
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA (B200) device")
-    config.addinivalue_line("markers", "slow: full-size case (minutes on CPU)")
 
 
 @pytest.fixture(scope="session")

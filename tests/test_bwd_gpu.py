@@ -1,0 +1,99 @@
+"""Backward parity of the CUDA path against the fp64 autograd restatement of
+the oracle (relative L2 <= 1e-2 per gradient), plus size-independent
+identities at the BASELINE training size."""
+import pytest
+import torch
+
+from oracle import cra_oracle as O
+from parity import GRAD_REL_L2, fwd_check, inputs, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+
+def _grads(q, k, v, do, dev, **kw):
+    import cron_root_attention as cra
+    qd, kd, vd = (t.to(dev).requires_grad_(True) for t in (q, k, v))
+    a = kw.pop("relay_log_scale", None)
+    ad = a.to(dev).requires_grad_(True) if a is not None else None
+    o = cra.cron_root_attention(qd, kd, vd, relay_log_scale=ad, **kw)
+    o.backward(do.to(dev))
+    torch.cuda.synchronize(dev)
+    assert cra.check_device_errors(dev) == 0
+    return o.detach(), qd.grad, kd.grad, vd.grad, (ad.grad if ad is not None else None)
+
+
+CASES = [
+    # B, Hq, Hkv, S, D, dtype, seed, top_k, alpha
+    (1, 2, 2, 1, 64, torch.float16, 0, 2, False),
+    (1, 1, 1, 17, 64, torch.bfloat16, 1, 2, False),
+    (1, 2, 2, 300, 64, torch.float16, 2, 2, False),
+    (1, 2, 2, 2304, 64, torch.float16, 3, 2, False),
+    (1, 1, 1, 3001, 128, torch.bfloat16, 4, 2, False),
+    (1, 4, 2, 2500, 64, torch.bfloat16, 5, 2, False),
+    (1, 2, 2, 2600, 128, torch.float16, 6, 2, True),
+    (2, 2, 2, 4100, 128, torch.bfloat16, 7, 2, False),
+    (1, 2, 2, 2200, 128, torch.float16, 8, 1, False),
+    (1, 2, 2, 2200, 64, torch.float16, 9, 3, False),
+]
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,S,D,dt,seed,top_k,alpha", CASES)
+def test_backward_vs_restatement(B, Hq, Hkv, S, D, dt, seed, top_k, alpha, cuda_device):
+    q, k, v, do = inputs(B, Hq, Hkv, S, D, dt, seed, with_do=True)
+    a = torch.linspace(-0.4, 0.4, Hkv) if alpha else None
+    o, dq, dk, dv, da = _grads(q, k, v, do, cuda_device, kv_groups=Hq // Hkv, relay_top_k=top_k,
+                               relay_log_scale=a)
+    ro, rdq, rdk, rdv, rda = O.forward_backward(q, k, v, do, kv_groups=Hq // Hkv, top_k=top_k,
+                                                relay_log_scale=a)
+    assert fwd_check(o, ro, dt)["ok"]
+    for name, x, y in (("dq", dq, rdq), ("dk", dk, rdk), ("dv", dv, rdv)):
+        assert rel_l2(x, y) <= GRAD_REL_L2, (name, rel_l2(x, y))
+    if alpha:
+        assert rel_l2(da, rda) <= GRAD_REL_L2
+
+
+def test_backward_deterministic(cuda_device):
+    q, k, v, do = inputs(1, 2, 2, 4100, 128, torch.bfloat16, 11, with_do=True)
+    r1 = _grads(q, k, v, do, cuda_device)
+    r2 = _grads(q, k, v, do, cuda_device)
+    for a, b in zip(r1[:4], r2[:4]):
+        assert torch.equal(a, b)
+
+
+def test_stride_zero_grad_output(cuda_device):
+    """o.sum().backward() hands the op an expanded (stride-0) dO."""
+    import cron_root_attention as cra
+    q, k, v = inputs(1, 2, 2, 2500, 64, torch.float16, 12)
+    qd, kd, vd = (t.to(cuda_device).requires_grad_(True) for t in (q, k, v))
+    cra.cron_root_attention(qd, kd, vd).float().sum().backward()
+    ones = torch.ones(1, 2, 2500, 64, dtype=torch.float16)
+    _, rdq, rdk, rdv, _ = O.forward_backward(q, k, v, ones)
+    for x, y in ((qd.grad, rdq), (kd.grad, rdk), (vd.grad, rdv)):
+        assert rel_l2(x, y) <= GRAD_REL_L2
+
+
+def test_config3_full_size(cuda_device):
+    """B2 H16 D128 S65536 bf16, seed 2, dO ~ N(0,1).
+    Checked through (a) sampled output rows and dQ rows against the oracle
+    (rows at the start, middle and end of one (b, h)) and (b) identities that
+    hold at any size: sum_j dV_j = sum_q dO_q and sum_j dK_j = 0 per (b, h)."""
+    dev = cuda_device
+    B, H, S, D = 2, 16, 65536, 128
+    q, k, v, do = inputs(B, H, H, S, D, torch.bfloat16, 2, with_do=True)
+    o, dq, dk, dv, _ = _grads(q, k, v, do, dev)
+    assert not any(torch.isnan(t).any().item() for t in (o, dq, dk, dv))
+    # (b) identities, in fp64 over every (b, h)
+    sdv = dv.double().sum(2).cpu()
+    sdo = do.double().sum(2)
+    assert rel_l2(sdv, sdo) <= GRAD_REL_L2
+    sdk = dk.double().sum(2).cpu()
+    assert (sdk.norm() / dk.double().norm().cpu()).item() <= 1e-2
+    # (a) sampled rows of (b=1, h=5)
+    bh = (slice(1, 2), slice(5, 6))
+    qs, ks, vs, dos = (t[bh] for t in (q, k, v, do))
+    for r0 in (0, 31744, S - 512):
+        rows = (r0, r0 + 512)
+        ro, _ = O.forward(qs, ks, vs, rows=rows)
+        assert fwd_check(o[bh][:, :, r0:r0 + 512], ro[:, :, r0:r0 + 512], torch.bfloat16)["ok"]
+        _, rdq, _, _, _ = O.forward_backward(qs, ks, vs, dos, rows=rows)
+        assert rel_l2(dq[bh][:, :, r0:r0 + 512], rdq[:, :, r0:r0 + 512]) <= GRAD_REL_L2

@@ -1,0 +1,168 @@
+"""Forward parity of the CUDA path (libcra through the public API and the C
+ABI) against the CPU oracle and the reference's golden vectors."""
+import ctypes
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import cra_oracle as O
+from parity import fwd_check, inputs
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = sorted(glob.glob(os.path.join(os.path.dirname(__file__), "golden", "*.npz")))
+
+
+def _cra():
+    import cron_root_attention as cra
+    return cra
+
+
+def _run(q, k, v, dev, **kw):
+    cra = _cra()
+    o = cra.cron_root_attention(q.to(dev), k.to(dev), v.to(dev), **kw)
+    torch.cuda.synchronize(dev)
+    assert cra.check_device_errors(dev) == 0
+    return o
+
+
+@pytest.mark.parametrize("path", GOLDEN, ids=[os.path.basename(p) for p in GOLDEN])
+def test_golden_vectors(path, cuda_device):
+    from test_oracle import load_golden
+    q, k, v, out, use_relay = load_golden(path)
+    o = _run(q, k, v, cuda_device)
+    r = fwd_check(o, out, q.dtype)
+    assert r["ok"], r
+
+
+CASES = [
+    # B, H, S, D, dtype, seed, sigma
+    (1, 2, 1, 64, torch.float16, 0, 1.0),
+    (1, 2, 2, 64, torch.float16, 0, 1.0),
+    (1, 1, 17, 128, torch.bfloat16, 1, 1.0),
+    (1, 2, 128, 64, torch.float16, 2, 1.0),
+    (1, 2, 129, 128, torch.float16, 3, 1.0),
+    (1, 1, 255, 64, torch.bfloat16, 4, 1.0),
+    (2, 2, 2048, 64, torch.float16, 5, 1.0),
+    (1, 2, 2049, 128, torch.bfloat16, 6, 1.0),
+    (1, 1, 3001, 64, torch.float16, 7, 1.0),
+    (1, 2, 4096, 128, torch.bfloat16, 8, 1.0),
+    (2, 2, 5000, 128, torch.float16, 9, 0.5),
+]
+
+
+@pytest.mark.parametrize("B,H,S,D,dt,seed,sigma", CASES)
+def test_forward_vs_oracle(B, H, S, D, dt, seed, sigma, cuda_device):
+    q, k, v = inputs(B, H, H, S, D, dt, seed, sigma)
+    o = _run(q, k, v, cuda_device)
+    ref, _ = O.forward(q, k, v)
+    r = fwd_check(o, ref, dt)
+    assert r["ok"], r
+
+
+def test_config2_full_size(cuda_device):
+    """B1 H12 D64 S16384 fp16, N(0,1)*0.5, seed 1."""
+    q, k, v = inputs(1, 12, 12, 16384, 64, torch.float16, 1, 0.5)
+    o = _run(q, k, v, cuda_device)
+    ref, _ = O.forward(q, k, v)
+    r = fwd_check(o, ref, torch.float16)
+    assert r["ok"], r
+
+
+@pytest.mark.parametrize("top_k", [1, 3, 4])
+def test_relay_top_k(top_k, cuda_device):
+    q, k, v = inputs(1, 2, 2, 2600, 64, torch.float16, 20 + top_k)
+    o = _run(q, k, v, cuda_device, relay_top_k=top_k)
+    ref, _ = O.forward(q, k, v, top_k=top_k)
+    assert fwd_check(o, ref, torch.float16)["ok"]
+
+
+def test_relay_log_scale_forward(cuda_device):
+    q, k, v = inputs(1, 2, 2, 2600, 128, torch.float16, 30)
+    a = torch.tensor([0.3, -0.5])
+    o = _run(q, k, v, cuda_device, relay_log_scale=a.to(cuda_device))
+    ref, _ = O.forward(q, k, v, relay_log_scale=a.half().float())
+    assert fwd_check(o, ref, torch.float16)["ok"]
+
+
+def test_gqa_forward(cuda_device):
+    q, k, v = inputs(1, 4, 2, 2500, 64, torch.bfloat16, 31)
+    o = _run(q, k, v, cuda_device, kv_groups=2)
+    ref, _ = O.forward(q, k, v, kv_groups=2)
+    assert fwd_check(o, ref, torch.bfloat16)["ok"]
+
+
+def test_non_contiguous_inputs(cuda_device):
+    """[B, S, H, D] storage viewed as [B, H, S, D] (what the modules pass)."""
+    g = torch.Generator().manual_seed(32)
+    x = torch.randn(3, 1, 2300, 2, 64, generator=g).half()
+    q, k, v = (x[i].transpose(1, 2) for i in range(3))
+    o = _run(q, k, v, cuda_device)
+    ref, _ = O.forward(q, k, v)
+    assert fwd_check(o, ref, torch.float16)["ok"]
+
+
+def test_small_head_dim_and_fp32_inputs(cuda_device):
+    q, k, v = inputs(1, 2, 2, 700, 32, torch.float32, 33)
+    o = _run(q, k, v, cuda_device)
+    assert o.dtype == torch.float32 and o.shape == q.shape
+    ref, _ = O.forward(q.bfloat16(), k.bfloat16(), v.bfloat16())
+    assert fwd_check(o.bfloat16(), ref, torch.bfloat16)["ok"]
+
+
+def test_lse_and_relay_rows_through_c_abi(cuda_device):
+    """Calls the C ABI directly: G rows / sources equal the oracle's top-k
+    selection (exact), and the lse matches the oracle's."""
+    from cron_root_attention import _lib
+    L = _lib.lib()
+    dev = cuda_device
+    B, H, S, D = 1, 2, 3001, 128
+    q, k, v = inputs(B, H, H, S, D, torch.bfloat16, 34)
+    qd, kd, vd = (t.to(dev) for t in (q, k, v))
+    W = L.cra_window(S)
+    NB = (S + W - 1) // W
+    NG = L.cra_global_rows(S, 1, 2)
+    gk = torch.empty(B, H, NG, D, device=dev, dtype=torch.bfloat16)
+    gv = torch.empty_like(gk)
+    gsrc = torch.empty(B, H, NB, 2, device=dev, dtype=torch.int32)
+    st = _lib.strides3
+    s = torch.cuda.current_stream(dev).cuda_stream
+    _lib.check(L.cra_relay_build(kd.data_ptr(), vd.data_ptr(), st(kd), st(vd), B, H, S, D, 1, 1, 2, None,
+                                 gk.data_ptr(), gv.data_ptr(), gsrc.data_ptr(), s), "relay")
+    o = torch.empty_like(qd)
+    lse = torch.empty(B, H, S, device=dev, dtype=torch.float32)
+    _lib.check(L.cra_fwd(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), gk.data_ptr(), gv.data_ptr(), st(qd), st(kd),
+                         st(vd), B, H, H, S, D, 1, 1, 2, ctypes.c_float(D ** -0.5), o.data_ptr(), st(o),
+                         lse.data_ptr(), None, s), "fwd")
+    torch.cuda.synchronize(dev)
+    ridx = O.relay_select(k, W, 2)
+    assert torch.equal(gsrc.cpu().long(), ridx)
+    rows = gk.cpu().view(B, H, NB, 3, D)
+    idx = torch.arange(NB) * W
+    assert torch.equal(rows[:, :, :, 0], k[:, :, idx])
+    for t in range(2):
+        assert torch.equal(rows[:, :, :, 1 + t], torch.gather(k, 2, ridx[..., t, None].expand(B, H, NB, D)))
+    ref_o, ref_lse = O.forward(q, k, v)
+    assert (lse.cpu() - ref_lse).abs().max().item() < 2e-3
+    assert fwd_check(o, ref_o, torch.bfloat16)["ok"]
+
+
+def test_deterministic(cuda_device):
+    q, k, v = inputs(1, 2, 2, 4100, 128, torch.bfloat16, 35)
+    a = _run(q, k, v, cuda_device)
+    b = _run(q, k, v, cuda_device)
+    assert torch.equal(a, b)
+
+
+def test_varlen_matches_per_document(cuda_device):
+    cra = _cra()
+    q, k, v = inputs(1, 2, 2, 5000, 64, torch.float16, 36)
+    cu = [0, 1000, 3100, 5000]
+    qd, kd, vd = (t.to(cuda_device) for t in (q, k, v))
+    o = cra.cron_root_attention_varlen(qd, kd, vd, torch.tensor(cu))
+    for s0, s1 in zip(cu, cu[1:]):
+        ref, _ = O.forward(q[:, :, s0:s1], k[:, :, s0:s1], v[:, :, s0:s1])
+        assert fwd_check(o[:, :, s0:s1], ref, torch.float16)["ok"]
