@@ -127,11 +127,15 @@ def _gather_rows(x: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
 def forward(q, k, v, *, use_relay: Optional[bool] = None, top_k: int = 2,
             relay_log_scale: Optional[torch.Tensor] = None,
             relay_idx: Optional[torch.Tensor] = None, W: Optional[int] = None,
-            chunk: int = 256, dtype=torch.float32, kv_groups: int = 1, rows=None):
+            chunk: int = 256, dtype=torch.float32, kv_groups: int = 1, rows=None,
+            relay_dtype=None):
     """Forward restatement of cpu_reference.py:198-339 (``cra_cpu_fast``).
 
     ``rows=(r0, r1)`` computes only query rows [r0, r1) (others are left 0);
     each row depends only on its own keys, so those rows are exact.
+    ``relay_dtype``: the reference keeps the scaled relay rows in the input
+    dtype (``relay_k * exp(a).to(dtype)``, core.py:3541-3544); pass that dtype
+    to round them the same way (the scale exp(a) is rounded too).
 
     Same chunked single-pass softmax: per chunk of ``chunk`` queries, scores
     against the local window and against the concatenated strided+relay rows,
@@ -156,11 +160,16 @@ def forward(q, k, v, *, use_relay: Optional[bool] = None, top_k: int = 2,
     Kg = _gather_rows(k, gl.idx)
     Vg = _gather_rows(v, gl.idx)
     if relay_log_scale is not None and use_relay:
-        f = torch.where(gl.is_relay.view(1, 1, -1, 1),
-                        relay_log_scale.to(dtype).exp().view(1, Hq, 1, 1),
+        e = relay_log_scale.to(dtype).exp()
+        if relay_dtype is not None:
+            e = relay_log_scale.float().exp().to(relay_dtype)
+        f = torch.where(gl.is_relay.view(1, 1, -1, 1), e.to(dtype).view(1, Hq, 1, 1),
                         torch.ones((), dtype=dtype))
         Kg = Kg * f
         Vg = Vg * f
+        if relay_dtype is not None:
+            Kg = Kg.to(relay_dtype).to(dtype)
+            Vg = Vg.to(relay_dtype).to(dtype)
     out = torch.zeros(B, Hq, S, D, dtype=dtype)
     lse = torch.zeros(B, Hq, S, dtype=dtype)
     pos = torch.arange(S)
@@ -192,7 +201,8 @@ def forward(q, k, v, *, use_relay: Optional[bool] = None, top_k: int = 2,
 def forward_backward(q, k, v, do, *, use_relay: Optional[bool] = None, top_k: int = 2,
                      relay_log_scale: Optional[torch.Tensor] = None,
                      relay_idx: Optional[torch.Tensor] = None, W: Optional[int] = None,
-                     chunk: int = 256, dtype=torch.float64, kv_groups: int = 1, rows=None):
+                     chunk: int = 256, dtype=torch.float64, kv_groups: int = 1, rows=None,
+                     relay_dtype=None):
     """Differentiable restatement; returns (out, dq, dk, dv, d_relay_log_scale).
 
     ``rows=(r0, r1)`` restricts the loss to query rows [r0, r1): dq of those
@@ -228,10 +238,15 @@ def forward_backward(q, k, v, do, *, use_relay: Optional[bool] = None, top_k: in
     Kg = _gather_rows(kk, gl.idx)
     Vg = _gather_rows(vv, gl.idx)
     if al is not None and use_relay:
-        f = torch.where(gl.is_relay.view(1, 1, -1, 1), al.exp().view(1, Hq, 1, 1),
-                        torch.ones((), dtype=dtype))
+        e = al.exp()
+        if relay_dtype is not None:  # value rounded as the reference does; gradient straight through
+            e = e + (e.detach().float().to(relay_dtype).to(dtype) - e.detach())
+        f = torch.where(gl.is_relay.view(1, 1, -1, 1), e.view(1, Hq, 1, 1), torch.ones((), dtype=dtype))
         Kg = Kg * f
         Vg = Vg * f
+        if relay_dtype is not None:
+            Kg = Kg + (Kg.detach().float().to(relay_dtype).to(dtype) - Kg.detach())
+            Vg = Vg + (Vg.detach().float().to(relay_dtype).to(dtype) - Vg.detach())
     pos = torch.arange(S)
     outs = []
     r0, r1 = rows if rows is not None else (0, S)

@@ -44,8 +44,9 @@ def test_backward_vs_restatement(B, Hq, Hkv, S, D, dt, seed, top_k, alpha, cuda_
     o, dq, dk, dv, da = _grads(q, k, v, do, cuda_device, kv_groups=Hq // Hkv, relay_top_k=top_k,
                                relay_log_scale=a)
     ro, rdq, rdk, rdv, rda = O.forward_backward(q, k, v, do, kv_groups=Hq // Hkv, top_k=top_k,
-                                                relay_log_scale=a)
-    assert fwd_check(o, ro, dt)["ok"]
+                                                relay_log_scale=a, relay_dtype=dt if alpha else None)
+    _r = fwd_check(o, ro, dt)
+    assert _r["ok"], _r
     for name, x, y in (("dq", dq, rdq), ("dk", dk, rdk), ("dv", dv, rdv)):
         assert rel_l2(x, y) <= GRAD_REL_L2, (name, rel_l2(x, y))
     if alpha:
@@ -94,6 +95,7 @@ def test_config3_full_size(cuda_device):
     for r0 in (0, 31744, S - 512):
         rows = (r0, r0 + 512)
         ro, _ = O.forward(qs, ks, vs, rows=rows)
-        assert fwd_check(o[bh][:, :, r0:r0 + 512], ro[:, :, r0:r0 + 512], torch.bfloat16)["ok"]
+        _r = fwd_check(o[bh][:, :, r0:r0 + 512], ro[:, :, r0:r0 + 512], torch.bfloat16)
+        assert _r["ok"], _r
         _, rdq, _, _, _ = O.forward_backward(qs, ks, vs, dos, rows=rows)
         assert rel_l2(dq[bh][:, :, r0:r0 + 512], rdq[:, :, r0:r0 + 512]) <= GRAD_REL_L2

@@ -59,7 +59,7 @@ def test_forward_vs_oracle(B, H, S, D, dt, seed, sigma, cuda_device):
     q, k, v = inputs(B, H, H, S, D, dt, seed, sigma)
     o = _run(q, k, v, cuda_device)
     ref, _ = O.forward(q, k, v)
-    r = fwd_check(o, ref, dt)
+    r = fwd_check(o, ref, dt, v_rms=sigma)
     assert r["ok"], r
 
 
@@ -77,22 +77,25 @@ def test_relay_top_k(top_k, cuda_device):
     q, k, v = inputs(1, 2, 2, 2600, 64, torch.float16, 20 + top_k)
     o = _run(q, k, v, cuda_device, relay_top_k=top_k)
     ref, _ = O.forward(q, k, v, top_k=top_k)
-    assert fwd_check(o, ref, torch.float16)["ok"]
+    _r = fwd_check(o, ref, torch.float16)
+    assert _r["ok"], _r
 
 
 def test_relay_log_scale_forward(cuda_device):
     q, k, v = inputs(1, 2, 2, 2600, 128, torch.float16, 30)
     a = torch.tensor([0.3, -0.5])
     o = _run(q, k, v, cuda_device, relay_log_scale=a.to(cuda_device))
-    ref, _ = O.forward(q, k, v, relay_log_scale=a.half().float())
-    assert fwd_check(o, ref, torch.float16)["ok"]
+    ref, _ = O.forward(q, k, v, relay_log_scale=a, relay_dtype=torch.float16)
+    _r = fwd_check(o, ref, torch.float16)
+    assert _r["ok"], _r
 
 
 def test_gqa_forward(cuda_device):
     q, k, v = inputs(1, 4, 2, 2500, 64, torch.bfloat16, 31)
     o = _run(q, k, v, cuda_device, kv_groups=2)
     ref, _ = O.forward(q, k, v, kv_groups=2)
-    assert fwd_check(o, ref, torch.bfloat16)["ok"]
+    _r = fwd_check(o, ref, torch.bfloat16)
+    assert _r["ok"], _r
 
 
 def test_non_contiguous_inputs(cuda_device):
@@ -102,7 +105,8 @@ def test_non_contiguous_inputs(cuda_device):
     q, k, v = (x[i].transpose(1, 2) for i in range(3))
     o = _run(q, k, v, cuda_device)
     ref, _ = O.forward(q, k, v)
-    assert fwd_check(o, ref, torch.float16)["ok"]
+    _r = fwd_check(o, ref, torch.float16)
+    assert _r["ok"], _r
 
 
 def test_small_head_dim_and_fp32_inputs(cuda_device):
@@ -110,7 +114,8 @@ def test_small_head_dim_and_fp32_inputs(cuda_device):
     o = _run(q, k, v, cuda_device)
     assert o.dtype == torch.float32 and o.shape == q.shape
     ref, _ = O.forward(q.bfloat16(), k.bfloat16(), v.bfloat16())
-    assert fwd_check(o.bfloat16(), ref, torch.bfloat16)["ok"]
+    _r = fwd_check(o.bfloat16(), ref, torch.bfloat16)
+    assert _r["ok"], _r
 
 
 def test_lse_and_relay_rows_through_c_abi(cuda_device):
@@ -147,7 +152,8 @@ def test_lse_and_relay_rows_through_c_abi(cuda_device):
         assert torch.equal(rows[:, :, :, 1 + t], torch.gather(k, 2, ridx[..., t, None].expand(B, H, NB, D)))
     ref_o, ref_lse = O.forward(q, k, v)
     assert (lse.cpu() - ref_lse).abs().max().item() < 2e-3
-    assert fwd_check(o, ref_o, torch.bfloat16)["ok"]
+    _r = fwd_check(o, ref_o, torch.bfloat16)
+    assert _r["ok"], _r
 
 
 def test_deterministic(cuda_device):
@@ -165,4 +171,5 @@ def test_varlen_matches_per_document(cuda_device):
     o = cra.cron_root_attention_varlen(qd, kd, vd, torch.tensor(cu))
     for s0, s1 in zip(cu, cu[1:]):
         ref, _ = O.forward(q[:, :, s0:s1], k[:, :, s0:s1], v[:, :, s0:s1])
-        assert fwd_check(o[:, :, s0:s1], ref, torch.float16)["ok"]
+        _r = fwd_check(o[:, :, s0:s1], ref, torch.float16)
+        assert _r["ok"], _r
