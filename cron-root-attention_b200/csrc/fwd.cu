@@ -1,26 +1,28 @@
 // fwd.cu -- forward pass of the causal 3-phase sqrt(N) attention on sm_100a.
 //
-// One CTA computes one 128-query tile of one (b, h).  The keys it needs are
-//   * the local band: 128-key tiles ending at the diagonal (band_tiles()),
-//   * a prefix of the (b, h) global-row list (strided + relay rows, geom.cuh),
-// and the CTA streams them through ONE online softmax, exactly the reference
-// forward's three phases (core.py:907-1158) folded into one loop.
+// One CTA computes TWO consecutive 128-query tiles (A = [m0, m0+128),
+// B = [m0+128, m0+256)) of one (b, h).  The keys they need -- the local band
+// and a prefix of the (b, h) global-row list (strided + relay rows,
+// geom.cuh) -- are streamed ONCE through shared memory and used by both
+// tiles (PairSchedule), halving L2 -> SMEM traffic per FLOP compared with one
+// tile per CTA.  Each tile runs one online softmax over all its keys, i.e. the
+// reference forward's three phases (core.py:907-1158) folded into one loop.
 //
-// Warp roles (256 threads):
-//   warp 0      TMA producer: Q once, then K/V (or G_k/G_v) tiles into an
-//               NST-deep ring of shared-memory stages.
-//   warp 1      tcgen05 issuer (one thread): S = Q K^T into one of two TMEM
-//               score buffers, then O += P V into the TMEM accumulator.
-//               Also owns the TMEM allocation.
-//   warps 4-7   softmax: thread r owns query row r (= TMEM lane r).  Loads
-//               its score row from TMEM, masks it with per-row [lo, hi)
-//               column bounds, updates the running max / sum, writes P
-//               (bf16/f16, swizzled) to shared memory for the PV MMA.
-//               O is rescaled in TMEM only when the running max grows by
-//               more than 2^8 (the result is exact either way: p <= 256).
-//   warps 2-3   idle.
-// Pipelining: S for tile j+1 is issued before PV for tile j, so the tensor
-// core works on the next scores while the softmax warps process this tile.
+// Warp roles (320 threads):
+//   warp 0      TMA producer: Q_A, Q_B once, then K_j, V_j, K_j+1, ... into a
+//               ring of NSLOT 128-row slots (K and V tiles are separate
+//               ring entries).
+//   warp 1      tcgen05 issuer (one thread) + TMEM owner.  Per key tile j:
+//               S_A = Q_A K_j^T, S_B = Q_B K_j^T (each only if that tile
+//               needs K_j), then O_A += P_A V_{j-1}, O_B += P_B V_{j-1}.
+//   warps 2-5   softmax of tile A, warps 6-9 softmax of tile B: a thread owns
+//               one query row (TMEM lane = 32 * (warp % 4) + lane).  It loads
+//               its score row, masks it with per-row [lo, hi) column bounds,
+//               updates the running max / sum and writes P (bf16 / f16,
+//               swizzled) to shared memory.  O is rescaled in TMEM only when
+//               the running max grows by more than 2^8 (exact either way).
+// While one softmax warpgroup works on its scores the tensor core computes
+// the other tile's scores and the PV products (ping-pong).
 #include "geom.cuh"
 #include "params.h"
 #include "sm100.cuh"
@@ -29,44 +31,43 @@ namespace cra {
 
 template <int D>
 struct FwdCfg {
-  static constexpr int NST = (D == 128) ? 2 : 4;      // K/V ring depth
-  static constexpr int Q_BYTES = kTile * D * 2;
-  static constexpr int KV_BYTES = kTile * D * 2;     // one K (or V) tile
+  static constexpr int TB = kTile * D * 2;            // one [128 x D] tile
+  static constexpr int NSLOT = (D == 128) ? 3 : 6;    // K/V ring slots
   static constexpr int P_BYTES = kTile * kTile * 2;
-  static constexpr int OFF_Q = 0;
-  static constexpr int OFF_K = OFF_Q + Q_BYTES;
-  static constexpr int OFF_V = OFF_K + NST * KV_BYTES;
-  static constexpr int OFF_P = OFF_V + NST * KV_BYTES;
-  static constexpr int OFF_BAR = OFF_P + P_BYTES;
-  // barriers: Q_FULL, K_FULL[NST], V_FULL[NST], KV_EMPTY[NST], S_FULL[2],
-  // S_FREE[2], P_FULL, PV_DONE
+  static constexpr int OFF_Q = 0;                      // Q_A, Q_B
+  static constexpr int OFF_P = OFF_Q + 2 * TB;         // P_A, P_B
+  static constexpr int OFF_RING = OFF_P + 2 * P_BYTES;
+  static constexpr int OFF_BAR = OFF_RING + NSLOT * TB;
   static constexpr int B_QFULL = 0;
-  static constexpr int B_KFULL = 1;
-  static constexpr int B_VFULL = B_KFULL + NST;
-  static constexpr int B_EMPTY = B_VFULL + NST;
-  static constexpr int B_SFULL = B_EMPTY + NST;
-  static constexpr int B_SFREE = B_SFULL + 2;
-  static constexpr int B_PFULL = B_SFREE + 2;
-  static constexpr int B_PVDONE = B_PFULL + 1;
-  static constexpr int B_DRAIN = B_PVDONE + 1;
+  static constexpr int B_FULL = 1;                     // [NSLOT]
+  static constexpr int B_EMPTY = B_FULL + NSLOT;       // [NSLOT]
+  static constexpr int B_SFULL = B_EMPTY + NSLOT;      // [2] per query tile
+  static constexpr int B_SFREE = B_SFULL + 2;          // [2]
+  static constexpr int B_PFULL = B_SFREE + 2;          // [2]
+  static constexpr int B_PVDONE = B_PFULL + 2;         // [2]
+  static constexpr int B_DRAIN = B_PVDONE + 2;
   static constexpr int N_BAR = B_DRAIN + 1;
   static constexpr int OFF_MISC = OFF_BAR + N_BAR * 8;  // tmem slot, abort flag
   static constexpr int SMEM = OFF_MISC + 16 + 1024;     // + alignment slack
   static constexpr int TMEM_COLS = 512;
-  static constexpr int COL_S0 = 0, COL_S1 = 128, COL_O = 256;
+  // TMEM columns: S_A, S_B (128 each), then O_A, O_B (D each)
+  static constexpr int COL_S = 0, COL_O = 256;
+  static_assert(SMEM <= 232448, "shared memory budget");
 };
 
 template <int D, bool BF16>
-__global__ void __launch_bounds__(256, 1) fwd_kernel(const __grid_constant__ QueryPassParams p) {
+__global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ QueryPassParams p) {
   using C = FwdCfg<D>;
   using E = Elt<BF16>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = p.n_qtiles - 1 - static_cast<int>(blockIdx.x);  // longest tiles first
+  const int n_pairs = (p.S + 2 * kTile - 1) / (2 * kTile);
+  const int pr = n_pairs - 1 - static_cast<int>(blockIdx.x);  // longest pairs first
   const int h = blockIdx.y, b = blockIdx.z, hk = h / p.kv_groups;
-  const int m0 = qt * kTile;
+  const int m0 = pr * 2 * kTile;
   const int W = p.W, S = p.S, R = p.R;
+  const PairSchedule sch(m0, S, W, R);
 
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + C::OFF_BAR;
@@ -75,22 +76,18 @@ __global__ void __launch_bounds__(256, 1) fwd_kernel(const __grid_constant__ Que
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
   const Abort ab{abort_flag, p.err};
 
-  const int nband = band_tiles(m0, W);
-  const int ntiles = nband + global_tiles(m0, S, W, R);
-
   if (threadIdx.x == 0) {
     mbar_init(BAR(C::B_QFULL), 1);
-    for (int i = 0; i < C::NST; ++i) {
-      mbar_init(BAR(C::B_KFULL + i), 1);
-      mbar_init(BAR(C::B_VFULL + i), 1);
+    for (int i = 0; i < C::NSLOT; ++i) {
+      mbar_init(BAR(C::B_FULL + i), 1);
       mbar_init(BAR(C::B_EMPTY + i), 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(BAR(C::B_SFULL + i), 1);
-      mbar_init(BAR(C::B_SFREE + i), 128);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(BAR(C::B_SFULL + x), 1);
+      mbar_init(BAR(C::B_SFREE + x), 128);
+      mbar_init(BAR(C::B_PFULL + x), 128);
+      mbar_init(BAR(C::B_PVDONE + x), 1);
     }
-    mbar_init(BAR(C::B_PFULL), 128);
-    mbar_init(BAR(C::B_PVDONE), 1);
     mbar_init(BAR(C::B_DRAIN), 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -100,6 +97,7 @@ __global__ void __launch_bounds__(256, 1) fwd_kernel(const __grid_constant__ Que
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const int nload = 2 * sch.ntiles;  // ring entries: K_0, V_0, K_1, V_1, ...
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -109,37 +107,32 @@ __global__ void __launch_bounds__(256, 1) fwd_kernel(const __grid_constant__ Que
       tma_prefetch(&p.tm_v);
       tma_prefetch(&p.tm_gk);
       tma_prefetch(&p.tm_gv);
-      mbar_expect_tx(BAR(C::B_QFULL), C::Q_BYTES);
-      for (int c = 0; c < D / 64; ++c)
-        tma_load_4d(sbase + C::OFF_Q + c * kTile * 128, &p.tm_q, BAR(C::B_QFULL), c * 64, m0, h, b);
+      const int nq = sch.valid_b ? 2 : 1;
+      mbar_expect_tx(BAR(C::B_QFULL), nq * C::TB);
+      for (int x = 0; x < nq; ++x)
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_4d(sbase + C::OFF_Q + x * C::TB + c * kTile * 128, &p.tm_q, BAR(C::B_QFULL), c * 64,
+                      m0 + x * kTile, h, b);
       int issued = 0;
-      for (int j = 0; j < ntiles; ++j) {
-        const int st = j % C::NST;
-        if (j >= C::NST && !mbar_wait(BAR(C::B_EMPTY + st), ((j / C::NST) - 1) & 1, ab)) break;
-        const bool g = j >= nband;
-        const int row0 = g ? (j - nband) * kTile : m0 - j * kTile;
-        const CUtensorMap* mk = g ? &p.tm_gk : &p.tm_k;
-        const CUtensorMap* mv = g ? &p.tm_gv : &p.tm_v;
-        mbar_expect_tx(BAR(C::B_KFULL + st), C::KV_BYTES);
+      for (int i = 0; i < nload; ++i) {
+        const int sl = i % C::NSLOT;
+        if (i >= C::NSLOT && !mbar_wait(BAR(C::B_EMPTY + sl), ((i / C::NSLOT) - 1) & 1, ab)) break;
+        int row0;
+        bool g, ua, ub;
+        sch.tile(i >> 1, row0, g, ua, ub);
+        const bool is_v = i & 1;
+        const CUtensorMap* m = g ? (is_v ? &p.tm_gv : &p.tm_gk) : (is_v ? &p.tm_v : &p.tm_k);
+        mbar_expect_tx(BAR(C::B_FULL + sl), C::TB);
         for (int c = 0; c < D / 64; ++c)
-          tma_load_4d(sbase + C::OFF_K + st * C::KV_BYTES + c * kTile * 128, mk, BAR(C::B_KFULL + st), c * 64, row0,
-                      hk, b);
-        mbar_expect_tx(BAR(C::B_VFULL + st), C::KV_BYTES);
-        for (int c = 0; c < D / 64; ++c)
-          tma_load_4d(sbase + C::OFF_V + st * C::KV_BYTES + c * kTile * 128, mv, BAR(C::B_VFULL + st), c * 64, row0,
-                      hk, b);
+          tma_load_4d(sbase + C::OFF_RING + sl * C::TB + c * kTile * 128, m, BAR(C::B_FULL + sl), c * 64, row0, hk,
+                      b);
         ++issued;
       }
-      // Drain: do not leave the CTA while copies into its shared memory are
-      // still in flight (only reachable after an abort).
-      if (*abort_flag) {
-        for (int j = (issued > C::NST ? issued - C::NST : 0); j < issued; ++j) {
-          const int st = j % C::NST;
-          const uint64_t t0 = globaltimer();
-          while (!mbar_try(BAR(C::B_VFULL + st), (j / C::NST) & 1) && globaltimer() - t0 < CRA_WAIT_LIMIT_NS) {
-          }
-        }
-      }
+      // Do not leave while copies into this CTA's shared memory are in
+      // flight (only reachable after an abort).
+      if (*abort_flag)
+        for (int i = (issued > C::NSLOT ? issued - C::NSLOT : 0); i < issued; ++i)
+          mbar_wait_bounded(BAR(C::B_FULL + i % C::NSLOT), (i / C::NSLOT) & 1);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -147,79 +140,102 @@ __global__ void __launch_bounds__(256, 1) fwd_kernel(const __grid_constant__ Que
     if (lane == 0) {
       constexpr uint32_t ID_S = idesc_f16(BF16, kTile, kTile, false, false);
       constexpr uint32_t ID_O = idesc_f16(BF16, kTile, D, false, true);
-      const uint32_t qs = sbase + C::OFF_Q, ps = sbase + C::OFF_P;
       bool ok = mbar_wait(BAR(C::B_QFULL), 0, ab);
-      auto issue_pv = [&](int i) -> bool {
-        const int st = i % C::NST;
-        if (!mbar_wait(BAR(C::B_PFULL), i & 1, ab)) return false;
-        if (!mbar_wait(BAR(C::B_VFULL + st), (i / C::NST) & 1, ab)) return false;
-        tc_fence_after();
-        const uint32_t vs = sbase + C::OFF_V + st * C::KV_BYTES;
+      int ns[2] = {0, 0};   // score tiles issued per query tile
+      int npv[2] = {0, 0};  // PV products issued per query tile
+      auto issue_pv = [&](int j) -> bool {
+        int row0;
+        bool g, use[2];
+        sch.tile(j, row0, g, use[0], use[1]);
+        const int i = 2 * j + 1, sl = i % C::NSLOT;
+        if (!mbar_wait(BAR(C::B_FULL + sl), (i / C::NSLOT) & 1, ab)) return false;
+        const uint32_t vs = sbase + C::OFF_RING + sl * C::TB;
+        for (int x = 0; x < 2; ++x) {
+          if (!use[x]) continue;
+          if (!mbar_wait(BAR(C::B_PFULL + x), npv[x] & 1, ab)) return false;
+          tc_fence_after();
+          const uint32_t ps = sbase + C::OFF_P + x * C::P_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk) {
-          const uint64_t a = sdesc(ps + (kk >> 2) * kTile * 128 + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = sdesc(vs + kk * 16 * 128, kTile * 128, 1024);
-          mma_ss(tmem + C::COL_O, a, bd, ID_O, (i > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kTile / 16; ++kk) {
+            const uint64_t a = sdesc(ps + (kk >> 2) * kTile * 128 + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = sdesc(vs + kk * 16 * 128, kTile * 128, 1024);
+            mma_ss(tmem + C::COL_O + x * D, a, bd, ID_O, (npv[x] > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(BAR(C::B_PVDONE + x));
+          ++npv[x];
         }
-        mma_commit(BAR(C::B_PVDONE));
-        mma_commit(BAR(C::B_EMPTY + st));
+        mma_commit(BAR(C::B_EMPTY + sl));
         return true;
       };
-      for (int j = 0; ok && j < ntiles; ++j) {
-        const int st = j % C::NST, sb = j & 1;
-        if (!mbar_wait(BAR(C::B_KFULL + st), (j / C::NST) & 1, ab)) { ok = false; break; }
-        if (j >= 2 && !mbar_wait(BAR(C::B_SFREE + sb), ((j >> 1) - 1) & 1, ab)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t ks = sbase + C::OFF_K + st * C::KV_BYTES;
+      for (int j = 0; ok && j < sch.ntiles; ++j) {
+        int row0;
+        bool g, use[2];
+        sch.tile(j, row0, g, use[0], use[1]);
+        const int i = 2 * j, sl = i % C::NSLOT;
+        if (!mbar_wait(BAR(C::B_FULL + sl), (i / C::NSLOT) & 1, ab)) { ok = false; break; }
+        const uint32_t ks = sbase + C::OFF_RING + sl * C::TB;
+        for (int x = 0; x < 2 && ok; ++x) {
+          if (!use[x]) continue;
+          if (ns[x] > 0 && !mbar_wait(BAR(C::B_SFREE + x), (ns[x] - 1) & 1, ab)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t qs = sbase + C::OFF_Q + x * C::TB;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t a = sdesc(qs + (kk >> 2) * kTile * 128 + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = sdesc(ks + (kk >> 2) * kTile * 128 + (kk & 3) * 32, 16, 1024);
-          mma_ss(tmem + (sb ? C::COL_S1 : C::COL_S0), a, bd, ID_S, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * kTile * 128 + (kk & 3) * 32;
+            mma_ss(tmem + C::COL_S + x * kTile, sdesc(qs + off, 16, 1024), sdesc(ks + off, 16, 1024), ID_S,
+                   kk > 0 ? 1u : 0u);
+          }
+          mma_commit(BAR(C::B_SFULL + x));
+          ++ns[x];
         }
-        mma_commit(BAR(C::B_SFULL + sb));
+        if (!ok) break;
+        mma_commit(BAR(C::B_EMPTY + sl));
         if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
       }
-      if (ok) ok = issue_pv(ntiles - 1);
+      if (ok) ok = issue_pv(sch.ntiles - 1);
       if (!ok) {
         // aborting: let every MMA already issued finish before TMEM is freed
         mma_commit(BAR(C::B_DRAIN));
-        const uint64_t t0 = globaltimer();
-        while (!mbar_try(BAR(C::B_DRAIN), 0) && globaltimer() - t0 < CRA_WAIT_LIMIT_NS) {
-        }
+        mbar_wait_bounded(BAR(C::B_DRAIN), 0);
       }
     }
     __syncwarp();
-  } else if (warp >= 4) {
+  } else {
     // ------------------------------------------------------------ softmax
-    const int r = threadIdx.x - 128;
-    const int qi = m0 + r;
+    const int x = (warp - 2) >> 2;           // 0: tile A, 1: tile B
+    const int r = ((warp & 3) << 5) | lane;  // row = TMEM lane
+    const int qi = m0 + x * kTile + r;
+    const bool tile_ok = (x == 0) || sch.valid_b;
     const bool row_ok = qi < S;
     const int ls = local_start(qi, W);
     const int cnt = gcount(qi, W, R);
     const uint32_t lane_off = static_cast<uint32_t>(r & ~31) << 16;
+    const uint32_t scol = tmem + lane_off + C::COL_S + x * kTile;
+    const uint32_t ocol = tmem + lane_off + C::COL_O + x * D;
     const float sl = p.scale_log2;
     float m_run = -INFINITY, l_run = 0.f;
+    int n = 0;  // key tiles processed by this query tile
     bool ok = true;
-    for (int j = 0; j < ntiles; ++j) {
-      const int sb = j & 1;
-      if (!mbar_wait(BAR(C::B_SFULL + sb), (j >> 1) & 1, ab)) { ok = false; break; }
+    for (int j = 0; tile_ok && j < sch.ntiles; ++j) {
+      int row0;
+      bool g, ua, ub;
+      sch.tile(j, row0, g, ua, ub);
+      if (!(x == 0 ? ua : ub)) continue;
+      if (!mbar_wait(BAR(C::B_SFULL + x), n & 1, ab)) { ok = false; break; }
       tc_fence_after();
       float s[4][32];
-      const uint32_t scol = tmem + lane_off + (sb ? C::COL_S1 : C::COL_S0);
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(scol + 32 * c, s[c]);
       tmem_ld_wait();
       tc_fence_before();
-      mbar_arrive(BAR(C::B_SFREE + sb));
+      mbar_arrive(BAR(C::B_SFREE + x));
       int lo, hi;
-      if (j < nband) {
-        const int kb = m0 - j * kTile;
-        lo = ls - kb;
-        hi = qi - kb + 1;
+      if (!g) {
+        lo = ls - row0;
+        hi = qi - row0 + 1;
       } else {
         lo = 0;
-        hi = cnt - (j - nband) * kTile;
+        hi = cnt - row0;
       }
       if (!row_ok) { lo = 0; hi = 0; }
       lo = max(lo, 0);
@@ -258,11 +274,10 @@ __global__ void __launch_bounds__(256, 1) fwd_kernel(const __grid_constant__ Que
           sum += s[c][e];
         }
       l_run = l_run * factor + sum;
-      if (j > 0) {
-        if (!mbar_wait(BAR(C::B_PVDONE), (j - 1) & 1, ab)) { ok = false; break; }
+      if (n > 0) {
+        if (!mbar_wait(BAR(C::B_PVDONE + x), (n - 1) & 1, ab)) { ok = false; break; }
         tc_fence_after();
         if (any) {
-          const uint32_t ocol = tmem + lane_off + C::COL_O;
 #pragma unroll 1
           for (int c = 0; c < D / 32; ++c) {
             float o[32];
@@ -275,8 +290,7 @@ __global__ void __launch_bounds__(256, 1) fwd_kernel(const __grid_constant__ Que
           tmem_st_wait();
         }
       }
-      // P row -> shared memory, 128B-swizzled, two 64-key chunks
-      uint8_t* prow = smem + C::OFF_P;
+      uint8_t* prow = smem + C::OFF_P + x * C::P_BYTES;
 #pragma unroll
       for (int u = 0; u < 16; ++u) {
         const int c = u >> 2, e0 = (u & 3) * 8;
@@ -289,13 +303,13 @@ __global__ void __launch_bounds__(256, 1) fwd_kernel(const __grid_constant__ Que
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(BAR(C::B_PFULL));
+      mbar_arrive(BAR(C::B_PFULL + x));
+      ++n;
     }
     // ---------------------------------------------------------- epilogue
-    if (ok && mbar_wait(BAR(C::B_PVDONE), (ntiles - 1) & 1, ab)) {
+    if (tile_ok && ok && n > 0 && mbar_wait(BAR(C::B_PVDONE + x), (n - 1) & 1, ab)) {
       tc_fence_after();
       const float inv = 1.f / fmaxf(l_run, 1e-6f);
-      const uint32_t ocol = tmem + lane_off + C::COL_O;
       typename E::T* orow = reinterpret_cast<typename E::T*>(p.out) + b * p.out_sb + h * p.out_sh +
                             static_cast<int64_t>(qi) * p.out_ss;
 #pragma unroll 1
@@ -316,7 +330,8 @@ __global__ void __launch_bounds__(256, 1) fwd_kernel(const __grid_constant__ Que
         }
       }
       if (row_ok)
-        p.lse[(static_cast<int64_t>(b) * p.H + h) * S + qi] = (m_run + log2f(fmaxf(l_run, 1e-6f))) * 0.69314718055994531f;
+        p.lse[(static_cast<int64_t>(b) * p.H + h) * S + qi] =
+            (m_run + log2f(fmaxf(l_run, 1e-6f))) * 0.69314718055994531f;
     }
   }
 
@@ -332,8 +347,8 @@ static cudaError_t launch_fwd_t(const QueryPassParams& p, cudaStream_t stream) {
   auto kern = fwd_kernel<D, BF16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
-  dim3 grid(p.n_qtiles, p.H, p.B);
-  kern<<<grid, 256, C::SMEM, stream>>>(p);
+  dim3 grid((p.S + 2 * kTile - 1) / (2 * kTile), p.H, p.B);
+  kern<<<grid, 320, C::SMEM, stream>>>(p);
   return cudaGetLastError();
 }
 

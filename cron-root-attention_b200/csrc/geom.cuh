@@ -68,4 +68,41 @@ __host__ __device__ __forceinline__ int first_query_seeing(int g, int S, int W, 
   return m < S ? (int)m : S;
 }
 
+// Key-tile schedule of a CTA that owns TWO consecutive 128-query tiles
+// A = [m0, m0+128) and B = [m0+128, m0+256) of one (b, h), sharing one stream
+// of 128-row key tiles.  Band tile t (t < nband) covers keys
+// [m0 + 128 - 128 t, m0 + 256 - 128 t) -- t = 0 is B's diagonal, t = 1 A's --
+// down to A's lowest local key (without a valid B, the list starts at t = 1).  Global tile g (after the band) covers global
+// rows [128 g, 128 g + 128).  use_a / use_b say which query tile needs the key
+// tile; every listed tile is needed by at least one of them.
+struct PairSchedule {
+  int m0, t0, nband, ntiles, lb, ca, cb;
+  bool valid_b;
+  __host__ __device__ __forceinline__ PairSchedule(int m0_, int S, int W, int R) : m0(m0_) {
+    valid_b = m0 + kTile < S;
+    const int la = local_start(m0, W);
+    lb = local_start(m0 + kTile, W);
+    t0 = valid_b ? 0 : 1;  // without B, B's diagonal tile is not needed
+    nband = (m0 + 2 * kTile - la + kTile - 1) / kTile - t0;
+    ca = gcount(min(m0 + kTile - 1, S - 1), W, R);
+    cb = valid_b ? gcount(min(m0 + 2 * kTile - 1, S - 1), W, R) : 0;
+    const int cmax = ca > cb ? ca : cb;
+    ntiles = nband + (cmax + kTile - 1) / kTile;
+  }
+  // row0: first key position (band) or first global row; g: global tile
+  __host__ __device__ __forceinline__ void tile(int j, int& row0, bool& g, bool& use_a, bool& use_b) const {
+    if (j < nband) {
+      g = false;
+      row0 = m0 + kTile - (j + t0) * kTile;
+      use_a = j + t0 >= 1;
+      use_b = valid_b && row0 + kTile > lb;
+    } else {
+      g = true;
+      row0 = (j - nband) * kTile;
+      use_a = row0 < ca;
+      use_b = row0 < cb;
+    }
+  }
+};
+
 }  // namespace cra
