@@ -74,28 +74,61 @@ __global__ void __launch_bounds__(256) delta_kernel(const void* __restrict__ op,
 }
 
 // ===========================================================================
-// dQ: query-centric, same key-tile sequence as the forward.
+// dQ: query-centric.  A CTA owns one 128-query tile and walks the forward's
+// key tiles (band, then global prefix) in 64-key units, skipping halves no row
+// needs.  Per unit: S = Q K_u^T and dP = dO V_u^T into one of two TMEM slots,
+// dS = P * (dP - Di) (P from the stored lse) -> shared memory, dQ += dS K_u.
+// The two softmax warpgroups take alternate units (the backward softmax has
+// no running state), so unit u+1's scores are computed while unit u is in
+// the softmax.
 // ===========================================================================
+struct DqUnits {
+  int m0, nband, ntiles, ls0, qmax, cmax;
+  __device__ __forceinline__ DqUnits(int m0_, int S, int W, int R) : m0(m0_) {
+    nband = band_tiles(m0, W);
+    ntiles = nband + global_tiles(m0, S, W, R);
+    ls0 = local_start(m0, W);
+    qmax = min(m0 + kTile - 1, S - 1);
+    cmax = gcount(qmax, W, R);
+  }
+  // half h of key tile j: first key row / global row, and whether any row of
+  // the tile needs it
+  __device__ __forceinline__ bool get(int j, int h, int& row0, bool& g) const {
+    if (j < nband) {
+      g = false;
+      row0 = m0 - j * kTile + kUnit * h;
+      return row0 <= qmax && row0 + kUnit > ls0;
+    }
+    g = true;
+    row0 = (j - nband) * kTile + kUnit * h;
+    return row0 < cmax;
+  }
+};
+
 template <int D>
 struct DqCfg {
-  static constexpr int NST = (D == 128) ? 2 : 4;
-  static constexpr int TB = kTile * D * 2;  // one [128 x D] tile
+  static constexpr int TB = kTile * D * 2;    // Q / dO tile
+  static constexpr int UB = kUnit * D * 2;    // one K or V unit
+  static constexpr int NST = (D == 128) ? 4 : 8;
+  static constexpr int DSB = kTile * kUnit * 2;  // dS per slot
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_DO = OFF_Q + TB;
   static constexpr int OFF_K = OFF_DO + TB;
-  static constexpr int OFF_V = OFF_K + NST * TB;
-  static constexpr int OFF_DS = OFF_V + NST * TB;
-  static constexpr int OFF_BAR = OFF_DS + kTile * kTile * 2;
+  static constexpr int OFF_V = OFF_K + NST * UB;
+  static constexpr int OFF_DS = OFF_V + NST * UB;
+  static constexpr int OFF_BAR = OFF_DS + 2 * DSB;
   static constexpr int B_QFULL = 0, B_KFULL = 1, B_VFULL = 1 + NST, B_EMPTY = 1 + 2 * NST;
-  static constexpr int B_SFULL = 1 + 3 * NST, B_SFREE = B_SFULL + 1, B_DSFULL = B_SFREE + 1,
-                       B_DQDONE = B_DSFULL + 1, B_DRAIN = B_DQDONE + 1, N_BAR = B_DRAIN + 1;
+  static constexpr int B_SFULL = 1 + 3 * NST, B_SFREE = B_SFULL + 2, B_DSFULL = B_SFREE + 2, B_DSFREE = B_DSFULL + 2,
+                       B_DONE = B_DSFREE + 2, B_DRAIN = B_DONE + 1, N_BAR = B_DRAIN + 1;
   static constexpr int OFF_MISC = OFF_BAR + N_BAR * 8;
   static constexpr int SMEM = OFF_MISC + 16 + 1024;
-  static constexpr int COL_S = 0, COL_DP = 128, COL_DQ = 256;
+  // TMEM: slot s -> S at 128 s, dP at 128 s + 64; dQ at 256
+  static constexpr int COL_DQ = 256;
+  static_assert(SMEM <= 232448, "shared memory budget");
 };
 
 template <int D, bool BF16>
-__global__ void __launch_bounds__(256, 1) dq_kernel(const __grid_constant__ QueryPassParams p) {
+__global__ void __launch_bounds__(320, 1) dq_kernel(const __grid_constant__ QueryPassParams p) {
   using C = DqCfg<D>;
   using E = Elt<BF16>;
   extern __shared__ uint8_t smem_raw[];
@@ -106,14 +139,13 @@ __global__ void __launch_bounds__(256, 1) dq_kernel(const __grid_constant__ Quer
   const int m0 = qt * kTile;
   const int W = p.W, S = p.S, R = p.R;
   const int Spad = p.n_qtiles * kTile;
+  const DqUnits un(m0, S, W, R);
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + C::OFF_BAR;
   auto BAR = [&](int i) { return bar0 + 8u * i; };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
   const Abort ab{abort_flag, p.err};
-  const int nband = band_tiles(m0, W);
-  const int ntiles = nband + global_tiles(m0, S, W, R);
 
   if (threadIdx.x == 0) {
     mbar_init(BAR(C::B_QFULL), 1);
@@ -122,10 +154,13 @@ __global__ void __launch_bounds__(256, 1) dq_kernel(const __grid_constant__ Quer
       mbar_init(BAR(C::B_VFULL + i), 1);
       mbar_init(BAR(C::B_EMPTY + i), 1);
     }
-    mbar_init(BAR(C::B_SFULL), 1);
-    mbar_init(BAR(C::B_SFREE), 128);
-    mbar_init(BAR(C::B_DSFULL), 128);
-    mbar_init(BAR(C::B_DQDONE), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(BAR(C::B_SFULL + s), 1);
+      mbar_init(BAR(C::B_SFREE + s), 128);
+      mbar_init(BAR(C::B_DSFULL + s), 128);
+      mbar_init(BAR(C::B_DSFREE + s), 1);
+    }
+    mbar_init(BAR(C::B_DONE), 1);
     mbar_init(BAR(C::B_DRAIN), 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -143,142 +178,174 @@ __global__ void __launch_bounds__(256, 1) dq_kernel(const __grid_constant__ Quer
         tma_load_4d(sbase + C::OFF_Q + c * kTile * 128, &p.tm_q, BAR(C::B_QFULL), c * 64, m0, h, b);
         tma_load_4d(sbase + C::OFF_DO + c * kTile * 128, &p.tm_do, BAR(C::B_QFULL), c * 64, m0, h, b);
       }
-      int issued = 0;
-      for (int j = 0; j < ntiles; ++j) {
-        const int st = j % C::NST;
-        if (j >= C::NST && !mbar_wait(BAR(C::B_EMPTY + st), ((j / C::NST) - 1) & 1, ab)) break;
-        const bool g = j >= nband;
-        const int row0 = g ? (j - nband) * kTile : m0 - j * kTile;
-        mbar_expect_tx(BAR(C::B_KFULL + st), C::TB);
-        for (int c = 0; c < D / 64; ++c)
-          tma_load_4d(sbase + C::OFF_K + st * C::TB + c * kTile * 128, g ? &p.tm_gk : &p.tm_k, BAR(C::B_KFULL + st),
-                      c * 64, row0, hk, b);
-        mbar_expect_tx(BAR(C::B_VFULL + st), C::TB);
-        for (int c = 0; c < D / 64; ++c)
-          tma_load_4d(sbase + C::OFF_V + st * C::TB + c * kTile * 128, g ? &p.tm_gv : &p.tm_v, BAR(C::B_VFULL + st),
-                      c * 64, row0, hk, b);
-        ++issued;
-      }
+      int u = 0;
+      bool ok = true;
+      for (int j = 0; ok && j < un.ntiles; ++j)
+        for (int hh = 0; hh < 2; ++hh) {
+          int row0;
+          bool g;
+          if (!un.get(j, hh, row0, g)) continue;
+          const int st = u % C::NST;
+          if (u >= C::NST && !mbar_wait(BAR(C::B_EMPTY + st), ((u / C::NST) - 1) & 1, ab)) { ok = false; break; }
+          mbar_expect_tx(BAR(C::B_KFULL + st), C::UB);
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_4d(sbase + C::OFF_K + st * C::UB + c * kUnit * 128, g ? &p.tm_gk : &p.tm_k,
+                        BAR(C::B_KFULL + st), c * 64, row0, hk, b);
+          mbar_expect_tx(BAR(C::B_VFULL + st), C::UB);
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_4d(sbase + C::OFF_V + st * C::UB + c * kUnit * 128, g ? &p.tm_gv : &p.tm_v,
+                        BAR(C::B_VFULL + st), c * 64, row0, hk, b);
+          ++u;
+        }
       if (*abort_flag)
-        for (int j = (issued > C::NST ? issued - C::NST : 0); j < issued; ++j)
-          mbar_wait_bounded(BAR(C::B_VFULL + j % C::NST), (j / C::NST) & 1);
+        for (int i = (u > C::NST ? u - C::NST : 0); i < u; ++i) {
+          mbar_wait_bounded(BAR(C::B_KFULL + i % C::NST), (i / C::NST) & 1);
+          mbar_wait_bounded(BAR(C::B_VFULL + i % C::NST), (i / C::NST) & 1);
+        }
     }
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t ID_S = idesc_f16(BF16, kTile, kTile, false, false);
+      constexpr uint32_t ID_S = idesc_f16(BF16, kTile, kUnit, false, false);
       constexpr uint32_t ID_Q = idesc_f16(BF16, kTile, D, false, true);
-      const uint32_t qs = sbase + C::OFF_Q, dos = sbase + C::OFF_DO, dss = sbase + C::OFF_DS;
+      const uint32_t qs = sbase + C::OFF_Q, dos = sbase + C::OFF_DO;
       bool ok = mbar_wait(BAR(C::B_QFULL), 0, ab);
       auto issue_dq = [&](int i) -> bool {
-        const int st = i % C::NST;
-        if (!mbar_wait(BAR(C::B_DSFULL), i & 1, ab)) return false;
+        const int st = i % C::NST, sl = i & 1;
+        if (!mbar_wait(BAR(C::B_DSFULL + sl), (i >> 1) & 1, ab)) return false;
         tc_fence_after();
-        const uint32_t ks = sbase + C::OFF_K + st * C::TB;
+        const uint32_t ks = sbase + C::OFF_K + st * C::UB, dss = sbase + C::OFF_DS + sl * C::DSB;
 #pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk) {
-          const uint64_t a = sdesc(dss + (kk >> 2) * kTile * 128 + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = sdesc(ks + kk * 16 * 128, kTile * 128, 1024);
+        for (int kk = 0; kk < kUnit / 16; ++kk) {
+          const uint64_t a = sdesc(dss + kk * 32, 16, 1024);
+          const uint64_t bd = sdesc(ks + kk * 16 * 128, kUnit * 128, 1024);
           mma_ss(tmem + C::COL_DQ, a, bd, ID_Q, (i > 0 || kk > 0) ? 1u : 0u);
         }
-        mma_commit(BAR(C::B_DQDONE));
+        mma_commit(BAR(C::B_DSFREE + sl));
         mma_commit(BAR(C::B_EMPTY + st));
         return true;
       };
-      for (int j = 0; ok && j < ntiles; ++j) {
-        const int st = j % C::NST;
-        if (!mbar_wait(BAR(C::B_KFULL + st), (j / C::NST) & 1, ab)) { ok = false; break; }
-        if (!mbar_wait(BAR(C::B_VFULL + st), (j / C::NST) & 1, ab)) { ok = false; break; }
-        if (j > 0 && !mbar_wait(BAR(C::B_SFREE), (j - 1) & 1, ab)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t ks = sbase + C::OFF_K + st * C::TB, vs = sbase + C::OFF_V + st * C::TB;
+      int u = 0;
+      for (int j = 0; ok && j < un.ntiles; ++j)
+        for (int hh = 0; ok && hh < 2; ++hh) {
+          int row0;
+          bool g;
+          if (!un.get(j, hh, row0, g)) continue;
+          const int st = u % C::NST, sl = u & 1;
+          if (!mbar_wait(BAR(C::B_KFULL + st), (u / C::NST) & 1, ab) ||
+              !mbar_wait(BAR(C::B_VFULL + st), (u / C::NST) & 1, ab) ||
+              (u >= 2 && !mbar_wait(BAR(C::B_SFREE + sl), ((u >> 1) - 1) & 1, ab))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t ks = sbase + C::OFF_K + st * C::UB, vs = sbase + C::OFF_V + st * C::UB;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kTile * 128 + (kk & 3) * 32;
-          mma_ss(tmem + C::COL_S, sdesc(qs + off, 16, 1024), sdesc(ks + off, 16, 1024), ID_S, kk > 0 ? 1u : 0u);
-          mma_ss(tmem + C::COL_DP, sdesc(dos + off, 16, 1024), sdesc(vs + off, 16, 1024), ID_S, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t qo = (kk >> 2) * kTile * 128 + (kk & 3) * 32;
+            const uint32_t ko = (kk >> 2) * kUnit * 128 + (kk & 3) * 32;
+            mma_ss(tmem + 128 * sl, sdesc(qs + qo, 16, 1024), sdesc(ks + ko, 16, 1024), ID_S, kk > 0 ? 1u : 0u);
+            mma_ss(tmem + 128 * sl + 64, sdesc(dos + qo, 16, 1024), sdesc(vs + ko, 16, 1024), ID_S,
+                   kk > 0 ? 1u : 0u);
+          }
+          mma_commit(BAR(C::B_SFULL + sl));
+          if (u > 0 && !issue_dq(u - 1)) { ok = false; break; }
+          ++u;
         }
-        mma_commit(BAR(C::B_SFULL));
-        if (j > 0 && !issue_dq(j - 1)) { ok = false; break; }
-      }
-      if (ok) ok = issue_dq(ntiles - 1);
+      if (ok && u > 0) ok = issue_dq(u - 1);
+      if (ok) mma_commit(BAR(C::B_DONE));
       if (!ok) {
         mma_commit(BAR(C::B_DRAIN));
         mbar_wait_bounded(BAR(C::B_DRAIN), 0);
       }
     }
     __syncwarp();
-  } else if (warp >= 4) {
-    const int r = threadIdx.x - 128;
+  } else {
+    const int w = (warp - 2) >> 2;           // softmax warpgroup: units with (u & 1) == w
+    const int r = ((warp & 3) << 5) | lane;  // query row = TMEM lane
     const int qi = m0 + r;
     const bool row_ok = qi < S;
     const int ls = local_start(qi, W);
     const int cnt = gcount(qi, W, R);
     const uint32_t lane_off = static_cast<uint32_t>(r & ~31) << 16;
-    const float sl = p.scale_log2;
+    const float sl2 = p.scale_log2;
     const int64_t rowi = (static_cast<int64_t>(b) * p.H + h) * Spad + qi;
     const float lse2 = p.lse[rowi];  // lse * log2(e), padded array
     const float di = p.delta[rowi];
+    uint8_t* dsrow = smem + C::OFF_DS + w * C::DSB;
     bool ok = true;
-    for (int j = 0; j < ntiles; ++j) {
-      if (!mbar_wait(BAR(C::B_SFULL), j & 1, ab)) { ok = false; break; }
-      tc_fence_after();
-      int lo, hi;
-      if (j < nband) {
-        const int kb = m0 - j * kTile;
-        lo = ls - kb;
-        hi = qi - kb + 1;
-      } else {
-        lo = 0;
-        hi = cnt - (j - nband) * kTile;
-      }
-      if (!row_ok) { lo = 0; hi = 0; }
-      uint32_t pk[64];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float s[32], dp[32];
-        tmem_ld32(tmem + lane_off + C::COL_S + 32 * c, s);
-        tmem_ld32(tmem + lane_off + C::COL_DP + 32 * c, dp);
-        tmem_ld_wait();
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const int col = 32 * c + e;
-          const float p0 = (col >= lo && col < hi) ? ex2(fmaf(s[e], sl, -lse2)) : 0.f;
-          const float p1 = (col + 1 >= lo && col + 1 < hi) ? ex2(fmaf(s[e + 1], sl, -lse2)) : 0.f;
-          pk[16 * c + e / 2] = E::pack(p0 * (dp[e] - di), p1 * (dp[e + 1] - di));
+    int u = 0;
+    for (int j = 0; ok && j < un.ntiles; ++j)
+      for (int hh = 0; hh < 2; ++hh) {
+        int row0;
+        bool g;
+        if (!un.get(j, hh, row0, g)) continue;
+        const int mine = (u & 1) == w;
+        const int uu = u++;
+        if (!mine) continue;
+        if (!mbar_wait(BAR(C::B_SFULL + w), (uu >> 1) & 1, ab) ||
+            (uu >= 2 && !mbar_wait(BAR(C::B_DSFREE + w), ((uu >> 1) - 1) & 1, ab))) {
+          ok = false;
+          break;
         }
-      }
-      tc_fence_before();
-      mbar_arrive(BAR(C::B_SFREE));
-      if (j > 0 && !mbar_wait(BAR(C::B_DQDONE), (j - 1) & 1, ab)) { ok = false; break; }
-      uint8_t* dsrow = smem + C::OFF_DS;
+        tc_fence_after();
+        int lo, hi;
+        if (!g) {
+          lo = ls - row0;
+          hi = qi - row0 + 1;
+        } else {
+          lo = 0;
+          hi = cnt - row0;
+        }
+        if (!row_ok) { lo = 0; hi = 0; }
 #pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        *reinterpret_cast<uint4*>(dsrow + sw128_off(r, u, kTile)) =
-            make_uint4(pk[4 * u + 0], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        for (int c = 0; c < 2; ++c) {
+          float s[32], dp[32];
+          tmem_ld32(tmem + lane_off + 128 * w + 32 * c, s);
+          tmem_ld32(tmem + lane_off + 128 * w + 64 + 32 * c, dp);
+          tmem_ld_wait();
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const int col = 32 * c + e;
+            const float p0 = (col >= lo && col < hi) ? ex2(fmaf(s[e], sl2, -lse2)) : 0.f;
+            const float p1 = (col + 1 >= lo && col + 1 < hi) ? ex2(fmaf(s[e + 1], sl2, -lse2)) : 0.f;
+            pk[e / 2] = E::pack(p0 * (dp[e] - di), p1 * (dp[e + 1] - di));
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(dsrow + r * 128 + (((4 * c + q) ^ (r & 7)) << 4)) =
+                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+        }
+        tc_fence_before();
+        mbar_arrive(BAR(C::B_SFREE + w));
+        fence_proxy_async_smem();
+        mbar_arrive(BAR(C::B_DSFULL + w));
       }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(BAR(C::B_DSFULL));
-    }
-    if (ok && mbar_wait(BAR(C::B_DQDONE), (ntiles - 1) & 1, ab)) {
+    // epilogue: warpgroup w writes columns [w * D/2, (w+1) * D/2) of dQ
+    if (ok && (u == 0 || mbar_wait(BAR(C::B_DONE), 0, ab))) {
       tc_fence_after();
       typename E::T* orow = reinterpret_cast<typename E::T*>(p.out) + b * p.out_sb + h * p.out_sh +
                             static_cast<int64_t>(qi) * p.out_ss;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = w * (D / 64); c < (w + 1) * (D / 64); ++c) {
         float o[32];
-        tmem_ld32(tmem + lane_off + C::COL_DQ + 32 * c, o);
-        tmem_ld_wait();
+        if (u > 0) {
+          tmem_ld32(tmem + lane_off + C::COL_DQ + 32 * c, o);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = 0.f;
+        }
         if (row_ok) {
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
+          for (int q = 0; q < 4; ++q) {
             uint4 v4;
-            v4.x = E::pack(o[8 * u + 0] * p.scale, o[8 * u + 1] * p.scale);
-            v4.y = E::pack(o[8 * u + 2] * p.scale, o[8 * u + 3] * p.scale);
-            v4.z = E::pack(o[8 * u + 4] * p.scale, o[8 * u + 5] * p.scale);
-            v4.w = E::pack(o[8 * u + 6] * p.scale, o[8 * u + 7] * p.scale);
-            *reinterpret_cast<uint4*>(orow + 32 * c + 8 * u) = v4;
+            v4.x = E::pack(o[8 * q + 0] * p.scale, o[8 * q + 1] * p.scale);
+            v4.y = E::pack(o[8 * q + 2] * p.scale, o[8 * q + 3] * p.scale);
+            v4.z = E::pack(o[8 * q + 4] * p.scale, o[8 * q + 5] * p.scale);
+            v4.w = E::pack(o[8 * q + 6] * p.scale, o[8 * q + 7] * p.scale);
+            *reinterpret_cast<uint4*>(orow + 32 * c + 8 * q) = v4;
           }
         }
       }
@@ -292,31 +359,37 @@ __global__ void __launch_bounds__(256, 1) dq_kernel(const __grid_constant__ Quer
 
 // ===========================================================================
 // Key-centric pass.  Thread r owns key row r of the CTA's 128-row key tile
-// (K/V rows in LOCAL mode, global rows G in GLOBAL mode).  Per query tile:
-//   S^T = K Q^T, dP^T = V dO^T  (TMEM),  P^T, dS^T -> shared memory,
-//   dV += P^T dO,  dK += dS^T Q  (TMEM accumulators).
+// (K/V rows in LOCAL mode, global rows G in GLOBAL mode).  The queries that
+// see the tile are walked in 64-query units; per unit:
+//   S^T = K Q_u^T, dP^T = V dO_u^T  (one of two TMEM slots),
+//   P^T, dS^T -> shared memory (per slot),
+//   dV += P^T dO_u,  dK += dS^T Q_u  (TMEM accumulators).
+// The two softmax warpgroups take alternate units.
 // ===========================================================================
 template <int D>
 struct KeyCfg {
-  static constexpr int NSQ = (D == 128) ? 1 : 2;  // Q/dO stages
-  static constexpr int TB = kTile * D * 2;
+  static constexpr int TB = kTile * D * 2;         // K or V tile
+  static constexpr int UB = kUnit * D * 2;         // Q or dO unit
+  static constexpr int NSQ = (D == 128) ? 3 : 6;   // Q/dO unit stages
+  static constexpr int PB = kTile * kUnit * 2;     // P^T (or dS^T) per slot
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + TB;
-  static constexpr int OFF_Q = OFF_V + TB;  // stage s: Q at OFF_Q + s*2*TB, dO after it
-  static constexpr int OFF_PT = OFF_Q + NSQ * 2 * TB;
-  static constexpr int OFF_DST = OFF_PT + kTile * kTile * 2;
-  static constexpr int OFF_LSE = OFF_DST + kTile * kTile * 2;  // stage s: lse2[128], delta[128]
-  static constexpr int OFF_BAR = OFF_LSE + NSQ * 2 * kTile * 4;
-  static constexpr int B_KVFULL = 0, B_QFULL = 1, B_QEMPTY = 1 + NSQ, B_SFULL = 1 + 2 * NSQ, B_SFREE = B_SFULL + 1,
-                       B_PFULL = B_SFREE + 1, B_MMADONE = B_PFULL + 1, B_DRAIN = B_MMADONE + 1,
+  static constexpr int OFF_Q = OFF_V + TB;         // stage s: Q at OFF_Q + 2 s UB, dO after it
+  static constexpr int OFF_PT = OFF_Q + NSQ * 2 * UB;  // slot s: P^T at OFF_PT + 2 s PB, dS^T after it
+  static constexpr int OFF_LSE = OFF_PT + 4 * PB;  // stage s: lse2[64], delta[64]
+  static constexpr int OFF_BAR = OFF_LSE + NSQ * 2 * kUnit * 4;
+  static constexpr int B_KVFULL = 0, B_QFULL = 1, B_QEMPTY = 1 + NSQ, B_SFULL = 1 + 2 * NSQ, B_SFREE = B_SFULL + 2,
+                       B_PFULL = B_SFREE + 2, B_PFREE = B_PFULL + 2, B_DONE = B_PFREE + 2, B_DRAIN = B_DONE + 1,
                        N_BAR = B_DRAIN + 1;
   static constexpr int OFF_MISC = OFF_BAR + N_BAR * 8;
   static constexpr int SMEM = OFF_MISC + 16 + 1024;
-  static constexpr int COL_ST = 0, COL_DPT = 128, COL_DV = 256, COL_DK = 256 + D;
+  // TMEM: slot s -> S^T at 128 s, dP^T at 128 s + 64; dV at 256, dK at 256 + D
+  static constexpr int COL_DV = 256, COL_DK = 256 + D;
+  static_assert(SMEM <= 232448, "shared memory budget");
 };
 
 template <int D, bool BF16, bool GLOBAL>
-__global__ void __launch_bounds__(256, 1) keypass_kernel(const __grid_constant__ KeyPassParams p) {
+__global__ void __launch_bounds__(320, 1) keypass_kernel(const __grid_constant__ KeyPassParams p) {
   using C = KeyCfg<D>;
   using E = Elt<BF16>;
   using T = typename E::T;
@@ -325,26 +398,25 @@ __global__ void __launch_bounds__(256, 1) keypass_kernel(const __grid_constant__
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hk = blockIdx.y, b = blockIdx.z;
   const int W = p.W, S = p.S, R = p.R;
-  const int n_qtiles = (S + kTile - 1) / kTile;
-  const int Spad = n_qtiles * kTile;
+  const int n_units = (S + kUnit - 1) / kUnit;
+  const int Spad = ((S + kTile - 1) / kTile) * kTile;
   const int groups = p.kv_groups;
 
-  // key tile and the query tiles [t_lo, t_hi) it meets (per group head)
+  // key tile and the 64-query units [t_lo, t_hi) it meets (per group head)
   int k0, split = 0, t_lo, t_hi;
   if (GLOBAL) {
     const int gt = static_cast<int>(blockIdx.x) / p.n_split;
     split = static_cast<int>(blockIdx.x) % p.n_split;
     k0 = gt * kTile;
-    const int qmin = first_query_seeing(k0, S, W, R);
-    const int tmin = qmin / kTile;
-    const int tot = n_qtiles - tmin;
+    const int tmin = first_query_seeing(k0, S, W, R) / kUnit;
+    const int tot = n_units - tmin;
     t_lo = tmin + static_cast<int>((static_cast<int64_t>(tot) * split) / p.n_split);
     t_hi = tmin + static_cast<int>((static_cast<int64_t>(tot) * (split + 1)) / p.n_split);
   } else {
     k0 = (p.n_ktiles - 1 - static_cast<int>(blockIdx.x)) * kTile;
     const int qlast = min(k0 + kTile - 1 + W - 1, S - 1);
-    t_lo = k0 / kTile;
-    t_hi = qlast / kTile + 1;
+    t_lo = k0 / kUnit;
+    t_hi = qlast / kUnit + 1;
   }
   const int nT = t_hi - t_lo;
   const int nU = nT * groups;
@@ -362,10 +434,13 @@ __global__ void __launch_bounds__(256, 1) keypass_kernel(const __grid_constant__
       mbar_init(BAR(C::B_QFULL + i), 1);
       mbar_init(BAR(C::B_QEMPTY + i), 1);
     }
-    mbar_init(BAR(C::B_SFULL), 1);
-    mbar_init(BAR(C::B_SFREE), 128);
-    mbar_init(BAR(C::B_PFULL), 128);
-    mbar_init(BAR(C::B_MMADONE), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(BAR(C::B_SFULL + s), 1);
+      mbar_init(BAR(C::B_SFREE + s), 128);
+      mbar_init(BAR(C::B_PFULL + s), 128);
+      mbar_init(BAR(C::B_PFREE + s), 1);
+    }
+    mbar_init(BAR(C::B_DONE), 1);
     mbar_init(BAR(C::B_DRAIN), 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -378,7 +453,7 @@ __global__ void __launch_bounds__(256, 1) keypass_kernel(const __grid_constant__
 
   auto unit = [&](int u, int& h, int& q0) {
     h = hk * groups + u / nT;
-    q0 = (t_lo + u % nT) * kTile;
+    q0 = (t_lo + u % nT) * kUnit;
   };
 
   if (warp == 0) {
@@ -394,16 +469,16 @@ __global__ void __launch_bounds__(256, 1) keypass_kernel(const __grid_constant__
         if (u >= C::NSQ && !mbar_wait(BAR(C::B_QEMPTY + st), ((u / C::NSQ) - 1) & 1, ab)) break;
         int h, q0;
         unit(u, h, q0);
-        const uint32_t qd = sbase + C::OFF_Q + st * 2 * C::TB;
-        mbar_expect_tx(BAR(C::B_QFULL + st), 2 * C::TB + 2 * kTile * 4);
+        const uint32_t qd = sbase + C::OFF_Q + st * 2 * C::UB;
+        mbar_expect_tx(BAR(C::B_QFULL + st), 2 * C::UB + 2 * kUnit * 4);
         for (int c = 0; c < D / 64; ++c) {
-          tma_load_4d(qd + c * kTile * 128, &p.tm_q, BAR(C::B_QFULL + st), c * 64, q0, h, b);
-          tma_load_4d(qd + C::TB + c * kTile * 128, &p.tm_do, BAR(C::B_QFULL + st), c * 64, q0, h, b);
+          tma_load_4d(qd + c * kUnit * 128, &p.tm_q, BAR(C::B_QFULL + st), c * 64, q0, h, b);
+          tma_load_4d(qd + C::UB + c * kUnit * 128, &p.tm_do, BAR(C::B_QFULL + st), c * 64, q0, h, b);
         }
         const int64_t li = (static_cast<int64_t>(b) * p.H + h) * Spad + q0;
-        const uint32_t ld = sbase + C::OFF_LSE + st * 2 * kTile * 4;
-        bulk_load(ld, p.lse + li, kTile * 4, BAR(C::B_QFULL + st));
-        bulk_load(ld + kTile * 4, p.delta + li, kTile * 4, BAR(C::B_QFULL + st));
+        const uint32_t ld = sbase + C::OFF_LSE + st * 2 * kUnit * 4;
+        bulk_load(ld, p.lse + li, kUnit * 4, BAR(C::B_QFULL + st));
+        bulk_load(ld + kUnit * 4, p.delta + li, kUnit * 4, BAR(C::B_QFULL + st));
         ++issued;
       }
       if (*abort_flag)
@@ -413,60 +488,62 @@ __global__ void __launch_bounds__(256, 1) keypass_kernel(const __grid_constant__
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0 && nU > 0) {
-      constexpr uint32_t ID_S = idesc_f16(BF16, kTile, kTile, false, false);
+      constexpr uint32_t ID_S = idesc_f16(BF16, kTile, kUnit, false, false);
       constexpr uint32_t ID_G = idesc_f16(BF16, kTile, D, false, true);
       const uint32_t ks = sbase + C::OFF_K, vs = sbase + C::OFF_V;
-      const uint32_t pts = sbase + C::OFF_PT, dsts = sbase + C::OFF_DST;
       bool ok = mbar_wait(BAR(C::B_KVFULL), 0, ab);
       auto issue_kv = [&](int i) -> bool {
-        const int st = i % C::NSQ;
-        if (!mbar_wait(BAR(C::B_PFULL), i & 1, ab)) return false;
+        const int st = i % C::NSQ, sl = i & 1;
+        if (!mbar_wait(BAR(C::B_PFULL + sl), (i >> 1) & 1, ab)) return false;
         tc_fence_after();
-        const uint32_t qd = sbase + C::OFF_Q + st * 2 * C::TB;
+        const uint32_t qd = sbase + C::OFF_Q + st * 2 * C::UB;
+        const uint32_t pts = sbase + C::OFF_PT + sl * 2 * C::PB, dsts = pts + C::PB;
 #pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * kTile * 128 + (kk & 3) * 32;
+        for (int kk = 0; kk < kUnit / 16; ++kk) {
           const uint32_t boff = kk * 16 * 128;
-          mma_ss(tmem + C::COL_DV, sdesc(pts + aoff, 16, 1024), sdesc(qd + C::TB + boff, kTile * 128, 1024), ID_G,
+          mma_ss(tmem + C::COL_DV, sdesc(pts + kk * 32, 16, 1024), sdesc(qd + C::UB + boff, kUnit * 128, 1024), ID_G,
                  (i > 0 || kk > 0) ? 1u : 0u);
-          mma_ss(tmem + C::COL_DK, sdesc(dsts + aoff, 16, 1024), sdesc(qd + boff, kTile * 128, 1024), ID_G,
+          mma_ss(tmem + C::COL_DK, sdesc(dsts + kk * 32, 16, 1024), sdesc(qd + boff, kUnit * 128, 1024), ID_G,
                  (i > 0 || kk > 0) ? 1u : 0u);
         }
-        mma_commit(BAR(C::B_MMADONE));
+        mma_commit(BAR(C::B_PFREE + sl));
         mma_commit(BAR(C::B_QEMPTY + st));
         return true;
       };
       for (int u = 0; ok && u < nU; ++u) {
-        const int st = u % C::NSQ;
-        // With one Q/dO stage the stage is refilled only after the previous
-        // unit's dV/dK MMAs release it, so those must be issued first.
-        if (C::NSQ == 1 && u > 0 && !issue_kv(u - 1)) { ok = false; break; }
-        if (!mbar_wait(BAR(C::B_QFULL + st), (u / C::NSQ) & 1, ab)) { ok = false; break; }
-        if (u > 0 && !mbar_wait(BAR(C::B_SFREE), (u - 1) & 1, ab)) { ok = false; break; }
+        const int st = u % C::NSQ, sl = u & 1;
+        if (!mbar_wait(BAR(C::B_QFULL + st), (u / C::NSQ) & 1, ab) ||
+            (u >= 2 && !mbar_wait(BAR(C::B_SFREE + sl), ((u >> 1) - 1) & 1, ab))) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const uint32_t qd = sbase + C::OFF_Q + st * 2 * C::TB;
+        const uint32_t qd = sbase + C::OFF_Q + st * 2 * C::UB;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kTile * 128 + (kk & 3) * 32;
-          mma_ss(tmem + C::COL_ST, sdesc(ks + off, 16, 1024), sdesc(qd + off, 16, 1024), ID_S, kk > 0 ? 1u : 0u);
-          mma_ss(tmem + C::COL_DPT, sdesc(vs + off, 16, 1024), sdesc(qd + C::TB + off, 16, 1024), ID_S,
+          const uint32_t ko = (kk >> 2) * kTile * 128 + (kk & 3) * 32;
+          const uint32_t qo = (kk >> 2) * kUnit * 128 + (kk & 3) * 32;
+          mma_ss(tmem + 128 * sl, sdesc(ks + ko, 16, 1024), sdesc(qd + qo, 16, 1024), ID_S, kk > 0 ? 1u : 0u);
+          mma_ss(tmem + 128 * sl + 64, sdesc(vs + ko, 16, 1024), sdesc(qd + C::UB + qo, 16, 1024), ID_S,
                  kk > 0 ? 1u : 0u);
         }
-        mma_commit(BAR(C::B_SFULL));
-        if (C::NSQ > 1 && u > 0 && !issue_kv(u - 1)) { ok = false; break; }
+        mma_commit(BAR(C::B_SFULL + sl));
+        if (u > 0 && !issue_kv(u - 1)) { ok = false; break; }
       }
       if (ok) ok = issue_kv(nU - 1);
+      if (ok) mma_commit(BAR(C::B_DONE));
       if (!ok) {
         mma_commit(BAR(C::B_DRAIN));
         mbar_wait_bounded(BAR(C::B_DRAIN), 0);
       }
     }
     __syncwarp();
-  } else if (warp >= 4) {
-    const int r = threadIdx.x - 128;
-    const int kj = k0 + r;  // key position (LOCAL) or global row (GLOBAL)
+  } else {
+    const int w = (warp - 2) >> 2;           // softmax warpgroup: units with (u & 1) == w
+    const int r = ((warp & 3) << 5) | lane;  // key row = TMEM lane
+    const int kj = k0 + r;                   // key position (LOCAL) or global row (GLOBAL)
     const uint32_t lane_off = static_cast<uint32_t>(r & ~31) << 16;
-    const float sl = p.scale_log2;
+    const float sl2 = p.scale_log2;
     // queries that see this key row: [qa, qb)
     int qa, qb;
     if (GLOBAL) {
@@ -476,76 +553,77 @@ __global__ void __launch_bounds__(256, 1) keypass_kernel(const __grid_constant__
       qa = kj;
       qb = kj < S ? min(kj + W, S) : kj;
     }
+    uint8_t* ptrow = smem + C::OFF_PT + w * 2 * C::PB + r * 128;
     bool ok = true;
-    for (int u = 0; u < nU; ++u) {
+    for (int u = w; u < nU; u += 2) {
       const int st = u % C::NSQ;
       int h, q0;
       unit(u, h, q0);
-      if (!mbar_wait(BAR(C::B_QFULL + st), (u / C::NSQ) & 1, ab)) { ok = false; break; }
-      if (!mbar_wait(BAR(C::B_SFULL), u & 1, ab)) { ok = false; break; }
+      if (!mbar_wait(BAR(C::B_QFULL + st), (u / C::NSQ) & 1, ab) ||
+          !mbar_wait(BAR(C::B_SFULL + w), (u >> 1) & 1, ab) ||
+          (u >= 2 && !mbar_wait(BAR(C::B_PFREE + w), ((u >> 1) - 1) & 1, ab))) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       const int lo = qa - q0, hi = qb - q0;
-      const float* sm_lse = reinterpret_cast<const float*>(smem + C::OFF_LSE + st * 2 * kTile * 4);
-      const float* sm_di = sm_lse + kTile;
-      uint32_t ppk[64], dpk[64];
+      const float* sm_lse = reinterpret_cast<const float*>(smem + C::OFF_LSE + st * 2 * kUnit * 4);
+      const float* sm_di = sm_lse + kUnit;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         float s[32], dp[32];
-        tmem_ld32(tmem + lane_off + C::COL_ST + 32 * c, s);
-        tmem_ld32(tmem + lane_off + C::COL_DPT + 32 * c, dp);
+        tmem_ld32(tmem + lane_off + 128 * w + 32 * c, s);
+        tmem_ld32(tmem + lane_off + 128 * w + 64 + 32 * c, dp);
         tmem_ld_wait();
+        uint32_t ppk[16], dpk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
           const int col = 32 * c + e;
-          const float p0 = (col >= lo && col < hi) ? ex2(fmaf(s[e], sl, -sm_lse[col])) : 0.f;
-          const float p1 = (col + 1 >= lo && col + 1 < hi) ? ex2(fmaf(s[e + 1], sl, -sm_lse[col + 1])) : 0.f;
-          ppk[16 * c + e / 2] = E::pack(p0, p1);
-          dpk[16 * c + e / 2] = E::pack(p0 * (dp[e] - sm_di[col]), p1 * (dp[e + 1] - sm_di[col + 1]));
+          const float p0 = (col >= lo && col < hi) ? ex2(fmaf(s[e], sl2, -sm_lse[col])) : 0.f;
+          const float p1 = (col + 1 >= lo && col + 1 < hi) ? ex2(fmaf(s[e + 1], sl2, -sm_lse[col + 1])) : 0.f;
+          ppk[e / 2] = E::pack(p0, p1);
+          dpk[e / 2] = E::pack(p0 * (dp[e] - sm_di[col]), p1 * (dp[e + 1] - sm_di[col + 1]));
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t off = ((4 * c + q) ^ (r & 7)) << 4;
+          *reinterpret_cast<uint4*>(ptrow + off) = make_uint4(ppk[4 * q], ppk[4 * q + 1], ppk[4 * q + 2], ppk[4 * q + 3]);
+          *reinterpret_cast<uint4*>(ptrow + C::PB + off) =
+              make_uint4(dpk[4 * q], dpk[4 * q + 1], dpk[4 * q + 2], dpk[4 * q + 3]);
         }
       }
       tc_fence_before();
-      mbar_arrive(BAR(C::B_SFREE));
-      if (u > 0 && !mbar_wait(BAR(C::B_MMADONE), (u - 1) & 1, ab)) { ok = false; break; }
-#pragma unroll
-      for (int w = 0; w < 16; ++w) {
-        const uint32_t off = sw128_off(r, w, kTile);
-        *reinterpret_cast<uint4*>(smem + C::OFF_PT + off) =
-            make_uint4(ppk[4 * w], ppk[4 * w + 1], ppk[4 * w + 2], ppk[4 * w + 3]);
-        *reinterpret_cast<uint4*>(smem + C::OFF_DST + off) =
-            make_uint4(dpk[4 * w], dpk[4 * w + 1], dpk[4 * w + 2], dpk[4 * w + 3]);
-      }
+      mbar_arrive(BAR(C::B_SFREE + w));
       fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(BAR(C::B_PFULL));
+      mbar_arrive(BAR(C::B_PFULL + w));
     }
     // ------------------------------------------------------------ epilogue
+    // warpgroup 0 writes dK, warpgroup 1 writes dV
     const bool have = nU > 0;
-    if (ok && (!have || mbar_wait(BAR(C::B_MMADONE), (nU - 1) & 1, ab))) {
+    if (ok && (!have || mbar_wait(BAR(C::B_DONE), 0, ab))) {
       tc_fence_after();
+      const uint32_t acc = tmem + lane_off + (w == 0 ? C::COL_DK : C::COL_DV);
+      const float mul = w == 0 ? p.scale : 1.f;
       if (GLOBAL) {
         const bool row_ok = kj < p.NG;
-        const int64_t base =
-            ((static_cast<int64_t>(split) * p.B + b) * (gridDim.y) + hk) * static_cast<int64_t>(p.NG) * D +
-            static_cast<int64_t>(kj) * D;
+        float* dst = (w == 0 ? p.part_k : p.part_v) +
+                     ((static_cast<int64_t>(split) * p.B + b) * gridDim.y + hk) * static_cast<int64_t>(p.NG) * D +
+                     static_cast<int64_t>(kj) * D;
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
-          float vk[32], vv[32];
+          float v[32];
           if (have) {
-            tmem_ld32(tmem + lane_off + C::COL_DK + 32 * c, vk);
-            tmem_ld32(tmem + lane_off + C::COL_DV + 32 * c, vv);
+            tmem_ld32(acc + 32 * c, v);
             tmem_ld_wait();
           } else {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) vk[e] = vv[e] = 0.f;
+            for (int e = 0; e < 32; ++e) v[e] = 0.f;
           }
           if (row_ok) {
 #pragma unroll
-            for (int e = 0; e < 32; e += 4) {
-              *reinterpret_cast<float4*>(p.part_k + base + 32 * c + e) =
-                  make_float4(vk[e] * p.scale, vk[e + 1] * p.scale, vk[e + 2] * p.scale, vk[e + 3] * p.scale);
-              *reinterpret_cast<float4*>(p.part_v + base + 32 * c + e) =
-                  make_float4(vv[e], vv[e + 1], vv[e + 2], vv[e + 3]);
-            }
+            for (int e = 0; e < 32; e += 4)
+              *reinterpret_cast<float4*>(dst + 32 * c + e) =
+                  make_float4(v[e] * mul, v[e + 1] * mul, v[e + 2] * mul, v[e + 3] * mul);
           }
         }
       } else {
@@ -553,6 +631,7 @@ __global__ void __launch_bounds__(256, 1) keypass_kernel(const __grid_constant__
         // global-row gradients that belong to this key position
         const int blk = kj / W;
         const int64_t gbase = (static_cast<int64_t>(b) * gridDim.y + hk) * static_cast<int64_t>(p.NG);
+        const float* dg = w == 0 ? p.dgk : p.dgv;
         int grow[5];
         float gsc[5];
         int ng = 0;
@@ -574,41 +653,35 @@ __global__ void __launch_bounds__(256, 1) keypass_kernel(const __grid_constant__
               }
           }
         }
-        T* dkrow = reinterpret_cast<T*>(p.dk) + b * p.dk_sb + hk * p.dk_sh + static_cast<int64_t>(kj) * p.dk_ss;
-        T* dvrow = reinterpret_cast<T*>(p.dv) + b * p.dv_sb + hk * p.dv_sh + static_cast<int64_t>(kj) * p.dv_ss;
+        T* drow = w == 0 ? reinterpret_cast<T*>(p.dk) + b * p.dk_sb + hk * p.dk_sh + static_cast<int64_t>(kj) * p.dk_ss
+                         : reinterpret_cast<T*>(p.dv) + b * p.dv_sb + hk * p.dv_sh + static_cast<int64_t>(kj) * p.dv_ss;
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
-          float vk[32], vv[32];
-          tmem_ld32(tmem + lane_off + C::COL_DK + 32 * c, vk);
-          tmem_ld32(tmem + lane_off + C::COL_DV + 32 * c, vv);
+          float v[32];
+          tmem_ld32(acc + 32 * c, v);
           tmem_ld_wait();
           if (row_ok) {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) vk[e] *= p.scale;
-            for (int g = 0; g < ng; ++g) {
-              const float* gk = p.dgk + (gbase + grow[g]) * D + 32 * c;
-              const float* gv = p.dgv + (gbase + grow[g]) * D + 32 * c;
+            for (int e = 0; e < 32; ++e) v[e] *= mul;
+            for (int gi = 0; gi < ng; ++gi) {
+              const float* gr = dg + (gbase + grow[gi]) * D + 32 * c;
 #pragma unroll
               for (int e = 0; e < 32; e += 4) {
-                const float4 a = *reinterpret_cast<const float4*>(gk + e);
-                const float4 bb = *reinterpret_cast<const float4*>(gv + e);
-                vk[e] += gsc[g] * a.x; vk[e + 1] += gsc[g] * a.y; vk[e + 2] += gsc[g] * a.z; vk[e + 3] += gsc[g] * a.w;
-                vv[e] += gsc[g] * bb.x; vv[e + 1] += gsc[g] * bb.y; vv[e + 2] += gsc[g] * bb.z; vv[e + 3] += gsc[g] * bb.w;
+                const float4 a = *reinterpret_cast<const float4*>(gr + e);
+                v[e] += gsc[gi] * a.x;
+                v[e + 1] += gsc[gi] * a.y;
+                v[e + 2] += gsc[gi] * a.z;
+                v[e + 3] += gsc[gi] * a.w;
               }
             }
 #pragma unroll
-            for (int u4 = 0; u4 < 4; ++u4) {
-              uint4 a, bb;
-              a.x = E::pack(vk[8 * u4 + 0], vk[8 * u4 + 1]);
-              a.y = E::pack(vk[8 * u4 + 2], vk[8 * u4 + 3]);
-              a.z = E::pack(vk[8 * u4 + 4], vk[8 * u4 + 5]);
-              a.w = E::pack(vk[8 * u4 + 6], vk[8 * u4 + 7]);
-              bb.x = E::pack(vv[8 * u4 + 0], vv[8 * u4 + 1]);
-              bb.y = E::pack(vv[8 * u4 + 2], vv[8 * u4 + 3]);
-              bb.z = E::pack(vv[8 * u4 + 4], vv[8 * u4 + 5]);
-              bb.w = E::pack(vv[8 * u4 + 6], vv[8 * u4 + 7]);
-              *reinterpret_cast<uint4*>(dkrow + 32 * c + 8 * u4) = a;
-              *reinterpret_cast<uint4*>(dvrow + 32 * c + 8 * u4) = bb;
+            for (int q = 0; q < 4; ++q) {
+              uint4 a;
+              a.x = E::pack(v[8 * q + 0], v[8 * q + 1]);
+              a.y = E::pack(v[8 * q + 2], v[8 * q + 3]);
+              a.z = E::pack(v[8 * q + 4], v[8 * q + 5]);
+              a.w = E::pack(v[8 * q + 6], v[8 * q + 7]);
+              *reinterpret_cast<uint4*>(drow + 32 * c + 8 * q) = a;
             }
           }
         }
@@ -696,7 +769,7 @@ static cudaError_t launch_bwd_t(const BwdLaunch& L, cudaStream_t st) {
   {
     auto kern = keypass_kernel<D, BF16, true>;
     if ((e = set_smem(kern, KeyCfg<D>::SMEM)) != cudaSuccess) return e;
-    kern<<<dim3(n_gtiles * gp.n_split, Hkv, B), 256, KeyCfg<D>::SMEM, st>>>(gp);
+    kern<<<dim3(n_gtiles * gp.n_split, Hkv, B), 320, KeyCfg<D>::SMEM, st>>>(gp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   {
@@ -715,13 +788,13 @@ static cudaError_t launch_bwd_t(const BwdLaunch& L, cudaStream_t st) {
   {
     auto kern = keypass_kernel<D, BF16, false>;
     if ((e = set_smem(kern, KeyCfg<D>::SMEM)) != cudaSuccess) return e;
-    kern<<<dim3(lp.n_ktiles, Hkv, B), 256, KeyCfg<D>::SMEM, st>>>(lp);
+    kern<<<dim3(lp.n_ktiles, Hkv, B), 320, KeyCfg<D>::SMEM, st>>>(lp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   {
     auto kern = dq_kernel<D, BF16>;
     if ((e = set_smem(kern, DqCfg<D>::SMEM)) != cudaSuccess) return e;
-    kern<<<dim3(qp.n_qtiles, H, B), 256, DqCfg<D>::SMEM, st>>>(qp);
+    kern<<<dim3(qp.n_qtiles, H, B), 320, DqCfg<D>::SMEM, st>>>(qp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   return cudaSuccess;

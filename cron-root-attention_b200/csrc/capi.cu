@@ -81,9 +81,9 @@ int check_tensor(const char* name, const void* p, const int64_t* st, int dim0, i
   return CRA_OK;
 }
 
-// 4-D tensor map over [d1 (outer), d0, rows, D] with 128 x 64 boxes, 128B swizzle.
+// 4-D tensor map over [d1 (outer), d0, rows, D] with box_rows x 64 boxes, 128B swizzle.
 int make_tmap(const char* name, CUtensorMap* m, const void* base, bool bf16, int D, int64_t rows, int64_t d0,
-              int64_t d1, const int64_t* st) {
+              int64_t d1, const int64_t* st, int box_rows = kTile) {
   auto fn = encode_fn();
   if (!fn) return fail(CRA_ERR_DRIVER, "cuTensorMapEncodeTiled not available from the driver");
   cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(d0),
@@ -95,7 +95,7 @@ int make_tmap(const char* name, CUtensorMap* m, const void* base, bool bf16, int
   if (d1 <= 1) s_b = s_h * d0;
   cuuint64_t strides[3] = {static_cast<cuuint64_t>(s_rows * 2), static_cast<cuuint64_t>(s_h * 2),
                            static_cast<cuuint64_t>(s_b * 2)};
-  cuuint32_t box[4] = {64, static_cast<cuuint32_t>(kTile), 1, 1};
+  cuuint32_t box[4] = {64, static_cast<cuuint32_t>(box_rows), 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -324,11 +324,18 @@ int cra_bwd(const void* q, const void* k, const void* v, const void* o, const vo
   float* delta = reinterpret_cast<float*>(ws + lay.off_delta);
   QueryPassParams& qp = L.qp;
   CRA_TRY(make_tmap("q", &qp.tm_q, q, bf16, head_dim, seq_len, heads, batch, q_strides));
-  CRA_TRY(make_tmap("k", &qp.tm_k, k, bf16, head_dim, seq_len, kv_heads, batch, k_strides));
-  CRA_TRY(make_tmap("v", &qp.tm_v, v, bf16, head_dim, seq_len, kv_heads, batch, v_strides));
-  CRA_TRY(make_tmap("g_k", &qp.tm_gk, g_k, bf16, head_dim, NG, kv_heads, batch, g_st));
-  CRA_TRY(make_tmap("g_v", &qp.tm_gv, g_v, bf16, head_dim, NG, kv_heads, batch, g_st));
+  CRA_TRY(make_tmap("k", &qp.tm_k, k, bf16, head_dim, seq_len, kv_heads, batch, k_strides, kUnit));
+  CRA_TRY(make_tmap("v", &qp.tm_v, v, bf16, head_dim, seq_len, kv_heads, batch, v_strides, kUnit));
+  CRA_TRY(make_tmap("g_k", &qp.tm_gk, g_k, bf16, head_dim, NG, kv_heads, batch, g_st, kUnit));
+  CRA_TRY(make_tmap("g_v", &qp.tm_gv, g_v, bf16, head_dim, NG, kv_heads, batch, g_st, kUnit));
   CRA_TRY(make_tmap("d_o", &qp.tm_do, d_o, bf16, head_dim, seq_len, heads, batch, do_strides));
+  CUtensorMap tm_q64, tm_do64, tm_k128, tm_v128, tm_gk128, tm_gv128;
+  CRA_TRY(make_tmap("q", &tm_q64, q, bf16, head_dim, seq_len, heads, batch, q_strides, kUnit));
+  CRA_TRY(make_tmap("d_o", &tm_do64, d_o, bf16, head_dim, seq_len, heads, batch, do_strides, kUnit));
+  CRA_TRY(make_tmap("k", &tm_k128, k, bf16, head_dim, seq_len, kv_heads, batch, k_strides));
+  CRA_TRY(make_tmap("v", &tm_v128, v, bf16, head_dim, seq_len, kv_heads, batch, v_strides));
+  CRA_TRY(make_tmap("g_k", &tm_gk128, g_k, bf16, head_dim, NG, kv_heads, batch, g_st));
+  CRA_TRY(make_tmap("g_v", &tm_gv128, g_v, bf16, head_dim, NG, kv_heads, batch, g_st));
   qp.out = dq;
   qp.out_sb = dq_strides[0];
   qp.out_sh = dq_strides[1];
@@ -348,10 +355,10 @@ int cra_bwd(const void* q, const void* k, const void* v, const void* o, const vo
   qp.err = dev_error;
   for (int mode = 0; mode < 2; ++mode) {
     KeyPassParams& kp = mode ? L.local : L.global;
-    kp.tm_q = qp.tm_q;
-    kp.tm_do = qp.tm_do;
-    kp.tm_k = mode ? qp.tm_k : qp.tm_gk;
-    kp.tm_v = mode ? qp.tm_v : qp.tm_gv;
+    kp.tm_q = tm_q64;
+    kp.tm_do = tm_do64;
+    kp.tm_k = mode ? tm_k128 : tm_gk128;
+    kp.tm_v = mode ? tm_v128 : tm_gv128;
     kp.lse = lse2;
     kp.delta = delta;
     kp.dk = dk;

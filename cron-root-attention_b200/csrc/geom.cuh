@@ -26,6 +26,7 @@
 namespace cra {
 
 constexpr int kTile = 128;  // query rows per tile and key rows per tile
+constexpr int kUnit = 64;   // backward work unit: 64 keys (dQ pass) or 64 queries (key passes)
 
 struct Geom {
   int S;   // sequence length
