@@ -34,6 +34,10 @@ _SIGNATURES = {
     "cra_relay_build": (_i, [_vp, _vp, _i64p, _i64p, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp]),
     "cra_fwd": (_i, [_vp, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp,
                      _i64p, _vp, _vp, _vp]),
+    "cra_relay_build_shard": (_i, [_vp, _vp, _i64p, _i64p, _i, _i, ctypes.c_int64, ctypes.c_int64, _i, _i, _i, _i, _i,
+                                   _vp, _vp, _vp, _vp, _vp]),
+    "cra_fwd_shard": (_i, [_vp, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _i, _i, _i, ctypes.c_int64, ctypes.c_int64,
+                           _i, ctypes.c_int64, _i, _i, _i, _i, _i, _f, _vp, _i64p, _vp, _vp, _vp]),
     "cra_bwd_workspace_bytes": (ctypes.c_size_t, [_i, _i, _i, _i, _i, _i, _i]),
     "cra_bwd": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _i64p, _i64p,
                      _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _vp, _vp,

@@ -1,0 +1,169 @@
+"""Multi-GPU execution: one process per GPU, torch.distributed for plumbing.
+
+Two ways to spread the work, matching how the attention decomposes:
+
+* Head / batch sharding (``shard_units``): every (b, h) pair is independent,
+  so each rank runs the ordinary op on its slice -- no collective at all.
+
+* Sequence split (``seq_parallel_forward``): one very long sequence is cut
+  into W-block-aligned query ranges, one per rank.  A rank's queries need
+    - the local window: its own K/V rows plus the last W - 1 rows of the
+      previous rank (the halo), and
+    - the global rows (strided key + relay tokens of every W-block) of the
+      WHOLE sequence.
+  Each rank builds the global rows of its own blocks, then one all-gather
+  (NCCL over NVLink on GPUs) assembles the full list in every rank's memory;
+  the halo rows travel in a second small all-gather.  Everything lands in
+  local HBM before the forward kernel reads it.
+
+Reference: the reference package is single-GPU (no collectives); the
+decomposition follows the attention's own structure (geom.cuh in libcra).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+
+
+def window(seq_len: int) -> int:
+    """W = ceil(sqrt(seq_len)) (reference core.py:3479)."""
+    w = int(math.ceil(math.sqrt(seq_len)))
+    while (w - 1) * (w - 1) >= seq_len:
+        w -= 1
+    while w * w < seq_len:
+        w += 1
+    return w
+
+
+def shard_units(batch: int, heads: int, world: int, rank: int) -> Sequence[Tuple[int, int, int]]:
+    """(b, h0, h1) slices of the batch x heads grid owned by ``rank``: heads
+    split evenly when heads % world == 0, otherwise the flattened (b, h) grid
+    is split into near-equal contiguous runs."""
+    if heads % world == 0:
+        per = heads // world
+        return [(b, rank * per, (rank + 1) * per) for b in range(batch)]
+    total = batch * heads
+    u0, u1 = total * rank // world, total * (rank + 1) // world
+    out = []
+    u = u0
+    while u < u1:
+        b, h = divmod(u, heads)
+        h1 = min(heads, h + (u1 - u))
+        out.append((b, h, h1))
+        u += h1 - h
+    return out
+
+
+def seq_shard(seq_len: int, world: int, rank: int) -> Tuple[int, int]:
+    """Query range [begin, end) of ``rank`` for a sequence split across
+    ``world`` ranks: W-blocks split as evenly as possible, block-aligned."""
+    W = window(seq_len)
+    nb = (seq_len + W - 1) // W
+    if nb < world:
+        raise ValueError(f"{nb} W-blocks cannot be split across {world} ranks")
+    b0, b1 = nb * rank // world, nb * (rank + 1) // world
+    return b0 * W, min(b1 * W, seq_len)
+
+
+class LibcraShardOps:
+    """The two compute steps of the sequence split, on this GPU (libcra)."""
+
+    def relay_build_shard(self, k, v, seq_len, row_begin, use_relay, top_k, relay_log_scale):
+        from . import _lib
+        from .core import _dtype_code, _stream_ptr
+        L = _lib.lib()
+        B, Hkv, rows, D = k.shape
+        W = window(seq_len)
+        R = 1 + top_k if use_relay else 1
+        nblk = (rows + W - 1) // W
+        gk = torch.empty(B, Hkv, nblk * R, D, device=k.device, dtype=k.dtype)
+        gv = torch.empty_like(gk)
+        gsrc = torch.empty(B, Hkv, nblk, top_k, device=k.device, dtype=torch.int32)
+        alpha = relay_log_scale.float().contiguous() if relay_log_scale is not None else None
+        with torch.cuda.device(k.device):
+            _lib.check(L.cra_relay_build_shard(k.data_ptr(), v.data_ptr(), _lib.strides3(k), _lib.strides3(v), B, Hkv,
+                                               seq_len, row_begin, rows, D, _dtype_code(k.dtype), int(use_relay),
+                                               top_k, alpha.data_ptr() if alpha is not None else None,
+                                               gk.data_ptr(), gv.data_ptr(), gsrc.data_ptr(),
+                                               _stream_ptr(k.device)), "cra_relay_build_shard")
+        return gk, gv
+
+    def forward_shard(self, q, k, v, gk, gv, seq_len, q_begin, kv_begin, use_relay, top_k):
+        from . import _lib
+        from .core import _dtype_code, _err_word, _stream_ptr
+        L = _lib.lib()
+        B, H, q_len, D = q.shape
+        Hkv, kv_len = k.shape[1], k.shape[2]
+        o = torch.empty_like(q)
+        lse = torch.empty(B, H, q_len, device=q.device, dtype=torch.float32)
+        st = _lib.strides3
+        with torch.cuda.device(q.device):
+            _lib.check(L.cra_fwd_shard(q.data_ptr(), k.data_ptr(), v.data_ptr(), gk.data_ptr(), gv.data_ptr(),
+                                       st(q), st(k), st(v), B, H, Hkv, seq_len, q_begin, q_len, kv_begin, kv_len, D,
+                                       _dtype_code(q.dtype), int(use_relay), top_k, ctypes.c_float(D ** -0.5),
+                                       o.data_ptr(), st(o), lse.data_ptr(), _err_word(q.device).data_ptr(),
+                                       _stream_ptr(q.device)), "cra_fwd_shard")
+        return o
+
+
+def _all_gather_padded(x: torch.Tensor, dim: int, sizes: Sequence[int], group) -> torch.Tensor:
+    """Concatenate, along ``dim``, every rank's ``x`` (rank r contributes
+    sizes[r] rows); pads to the largest size for the collective."""
+    mx = max(sizes)
+    pad = mx - x.shape[dim]
+    if pad:
+        shape = list(x.shape)
+        shape[dim] = pad
+        x = torch.cat([x, x.new_zeros(shape)], dim=dim)
+    x = x.contiguous()
+    parts = [torch.empty_like(x) for _ in sizes]
+    dist.all_gather(parts, x, group=group)
+    return torch.cat([p.narrow(dim, 0, s) for p, s in zip(parts, sizes)], dim=dim)
+
+
+@torch.no_grad()
+def seq_parallel_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, seq_len: int,
+                         group=None, relay_top_k: int = 2, relay_log_scale: Optional[torch.Tensor] = None,
+                         ops=None) -> torch.Tensor:
+    """Forward of one sequence split across the ranks of ``group``.
+
+    q, k, v: this rank's rows, [B, H, end - begin, D] with (begin, end) =
+    seq_shard(seq_len, world, rank).  Returns this rank's output rows.
+    Collectives: two all-gathers (global rows, then the halo rows); no
+    data-dependent host synchronisation.
+    """
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    ops = ops or LibcraShardOps()
+    begin, end = seq_shard(seq_len, world, rank)
+    if q.shape[2] != end - begin or k.shape[2] != end - begin:
+        raise ValueError(f"rank {rank} owns rows [{begin}, {end}) but got {q.shape[2]}")
+    W = window(seq_len)
+    use_relay = seq_len > 2048  # reference core.py:2832,3507
+    R = 1 + relay_top_k if use_relay else 1
+    # 1) global rows of this rank's blocks, then the whole list everywhere
+    gk, gv = ops.relay_build_shard(k, v, seq_len, begin, use_relay, relay_top_k, relay_log_scale)
+    rows = [((e - b + W - 1) // W) * R for b, e in (seq_shard(seq_len, world, r) for r in range(world))]
+    gk = _all_gather_padded(gk, 2, rows, group)
+    gv = _all_gather_padded(gv, 2, rows, group)
+    # 2) halo: the last W - 1 K/V rows of the previous rank
+    halo = W - 1
+    tail_k = k[:, :, max(0, k.shape[2] - halo):]
+    tail_v = v[:, :, max(0, v.shape[2] - halo):]
+    sizes = [min(halo, e - b) for b, e in (seq_shard(seq_len, world, r) for r in range(world))]
+    hk = _all_gather_padded(tail_k, 2, sizes, group)
+    hv = _all_gather_padded(tail_v, 2, sizes, group)
+    if rank > 0:
+        off = sum(sizes[:rank - 1])
+        n = sizes[rank - 1]
+        kk = torch.cat([hk.narrow(2, off, n), k], dim=2).contiguous()
+        vv = torch.cat([hv.narrow(2, off, n), v], dim=2).contiguous()
+        kv_begin = begin - n
+    else:
+        kk, vv, kv_begin = k.contiguous(), v.contiguous(), 0
+    return ops.forward_shard(q.contiguous(), kk, vv, gk.contiguous(), gv.contiguous(), seq_len, begin, kv_begin,
+                             use_relay, relay_top_k)

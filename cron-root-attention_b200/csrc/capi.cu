@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <climits>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -18,8 +19,8 @@
 
 namespace cra {
 cudaError_t launch_relay_build(int D, bool bf16, const void* k, const void* v, const int64_t* ks, const int64_t* vs,
-                               int B, int Hkv, int S, int W, int top_k, int R, const float* log_scale, void* gk,
-                               void* gv, int32_t* gsrc, cudaStream_t stream);
+                               int B, int Hkv, int S, int W, int top_k, int R, int pos0, const float* log_scale,
+                               void* gk, void* gv, int32_t* gsrc, cudaStream_t stream);
 cudaError_t launch_fwd(const QueryPassParams& p, int D, bool bf16, cudaStream_t stream);
 }  // namespace cra
 
@@ -222,7 +223,7 @@ int cra_relay_build(const void* k, const void* v, const int64_t* k_strides, cons
   const int W = cra_window(seq_len);
   const int R = rows_per_block(use_relay, top_k);
   cudaError_t e = launch_relay_build(head_dim, dtype == CRA_BF16, k, v, k_strides, v_strides, batch, kv_heads,
-                                     seq_len, W, top_k, R, use_relay ? relay_log_scale : nullptr, g_k, g_v,
+                                     seq_len, W, top_k, R, 0, use_relay ? relay_log_scale : nullptr, g_k, g_v,
                                      use_relay ? g_src : nullptr, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? CRA_OK : fail(CRA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
 }
@@ -269,6 +270,9 @@ int cra_fwd(const void* q, const void* k, const void* v, const void* g_k, const 
   p.R = R;
   p.NG = NG;
   p.n_qtiles = (seq_len + kTile - 1) / kTile;
+  p.q_begin = 0;
+  p.q_len = seq_len;
+  p.kv_begin = 0;
   p.scale = softmax_scale;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   p.err = dev_error;
@@ -350,6 +354,9 @@ int cra_bwd(const void* q, const void* k, const void* v, const void* o, const vo
   qp.R = R;
   qp.NG = NG;
   qp.n_qtiles = (seq_len + kTile - 1) / kTile;
+  qp.q_begin = 0;
+  qp.q_len = seq_len;
+  qp.kv_begin = 0;
   qp.scale = softmax_scale;
   qp.scale_log2 = softmax_scale * 1.4426950408889634f;
   qp.err = dev_error;
@@ -410,6 +417,88 @@ int cra_bwd(const void* q, const void* k, const void* v, const void* o, const vo
     if (me != cudaSuccess) return fail(CRA_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(me));
   }
   cudaError_t e = launch_bwd(L, head_dim, bf16, st);
+  return e == cudaSuccess ? CRA_OK : fail(CRA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+}
+
+int cra_relay_build_shard(const void* k, const void* v, const int64_t* k_strides, const int64_t* v_strides,
+                          int batch, int kv_heads, int64_t seq_len, int64_t row_begin, int rows, int head_dim,
+                          int dtype, int use_relay, int top_k, const float* relay_log_scale, void* g_k, void* g_v,
+                          int32_t* g_src, void* stream) {
+  CRA_TRY(check_common(batch, kv_heads, kv_heads, rows, head_dim, dtype, top_k));
+  if (seq_len < 1 || seq_len > INT32_MAX) return fail(CRA_ERR_INVALID_ARGUMENT, "seq_len out of range");
+  const int W = cra_window(seq_len);
+  if (row_begin < 0 || row_begin % W != 0 || row_begin + rows > seq_len)
+    return fail(CRA_ERR_INVALID_ARGUMENT, "shard [%lld, %lld) must start on a multiple of W = %d inside the sequence",
+                static_cast<long long>(row_begin), static_cast<long long>(row_begin + rows), W);
+  if (row_begin + rows != seq_len && rows % W != 0)
+    return fail(CRA_ERR_INVALID_ARGUMENT, "only the last shard may end inside a W-block");
+  CRA_TRY(check_tensor("k", k, k_strides, batch, kv_heads));
+  CRA_TRY(check_tensor("v", v, v_strides, batch, kv_heads));
+  if (!g_k || !g_v) return fail(CRA_ERR_INVALID_ARGUMENT, "g_k / g_v: null pointer");
+  if (!aligned16(g_k) || !aligned16(g_v)) return fail(CRA_ERR_MISALIGNED, "g_k / g_v: not 16-byte aligned");
+  const int R = rows_per_block(use_relay, top_k);
+  cudaError_t e = launch_relay_build(head_dim, dtype == CRA_BF16, k, v, k_strides, v_strides, batch, kv_heads, rows,
+                                     W, top_k, R, static_cast<int>(row_begin),
+                                     use_relay ? relay_log_scale : nullptr, g_k, g_v, use_relay ? g_src : nullptr,
+                                     static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? CRA_OK : fail(CRA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+}
+
+int cra_fwd_shard(const void* q, const void* k, const void* v, const void* g_k, const void* g_v,
+                  const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, int batch, int heads,
+                  int kv_heads, int64_t seq_len, int64_t q_begin, int q_len, int64_t kv_begin, int kv_len,
+                  int head_dim, int dtype, int use_relay, int top_k, float softmax_scale, void* o,
+                  const int64_t* o_strides, float* lse, int* dev_error, void* stream) {
+  CRA_TRY(check_common(batch, heads, kv_heads, q_len, head_dim, dtype, top_k));
+  if (seq_len < 1 || seq_len > INT32_MAX) return fail(CRA_ERR_INVALID_ARGUMENT, "seq_len out of range");
+  const int W = cra_window(seq_len);
+  if (q_begin < 0 || q_begin + q_len > seq_len) return fail(CRA_ERR_INVALID_ARGUMENT, "query shard outside the sequence");
+  if (kv_begin < 0 || kv_len < 1 || kv_begin > q_begin - (W - 1) && kv_begin > 0)
+    return fail(CRA_ERR_INVALID_ARGUMENT, "K/V rows must start at or before q_begin - (W - 1) (the local window)");
+  if (kv_begin + kv_len < q_begin + q_len)
+    return fail(CRA_ERR_INVALID_ARGUMENT, "K/V rows must reach the last query of the shard");
+  CRA_TRY(check_tensor("q", q, q_strides, batch, heads));
+  CRA_TRY(check_tensor("k", k, k_strides, batch, kv_heads));
+  CRA_TRY(check_tensor("v", v, v_strides, batch, kv_heads));
+  CRA_TRY(check_tensor("o", o, o_strides, batch, heads));
+  if (!g_k || !g_v || !lse) return fail(CRA_ERR_INVALID_ARGUMENT, "g_k / g_v / lse: null pointer");
+  if (!aligned16(g_k) || !aligned16(g_v)) return fail(CRA_ERR_MISALIGNED, "g_k / g_v: not 16-byte aligned");
+  if (!(softmax_scale > 0.f) || !std::isfinite(softmax_scale))
+    return fail(CRA_ERR_INVALID_ARGUMENT, "softmax_scale must be finite and > 0");
+  const bool bf16 = dtype == CRA_BF16;
+  const int R = rows_per_block(use_relay, top_k);
+  const int NG = static_cast<int>(cra_global_rows(seq_len, use_relay, top_k));
+  const int64_t g_st[3] = {static_cast<int64_t>(kv_heads) * NG * head_dim, static_cast<int64_t>(NG) * head_dim,
+                           head_dim};
+  CRA_TRY(bind_context());
+  QueryPassParams p;
+  std::memset(&p, 0, sizeof(p));
+  CRA_TRY(make_tmap("q", &p.tm_q, q, bf16, head_dim, q_len, heads, batch, q_strides));
+  CRA_TRY(make_tmap("k", &p.tm_k, k, bf16, head_dim, kv_len, kv_heads, batch, k_strides));
+  CRA_TRY(make_tmap("v", &p.tm_v, v, bf16, head_dim, kv_len, kv_heads, batch, v_strides));
+  CRA_TRY(make_tmap("g_k", &p.tm_gk, g_k, bf16, head_dim, NG, kv_heads, batch, g_st));
+  CRA_TRY(make_tmap("g_v", &p.tm_gv, g_v, bf16, head_dim, NG, kv_heads, batch, g_st));
+  p.tm_do = p.tm_q;
+  p.out = o;
+  p.out_sb = o_strides[0];
+  p.out_sh = o_strides[1];
+  p.out_ss = o_strides[2];
+  p.lse = lse;
+  p.B = batch;
+  p.H = heads;
+  p.kv_groups = heads / kv_heads;
+  p.S = static_cast<int>(seq_len);
+  p.W = W;
+  p.R = R;
+  p.NG = NG;
+  p.n_qtiles = (q_len + kTile - 1) / kTile;
+  p.q_begin = static_cast<int>(q_begin);
+  p.q_len = q_len;
+  p.kv_begin = static_cast<int>(kv_begin);
+  p.scale = softmax_scale;
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.err = dev_error;
+  cudaError_t e = launch_fwd(p, head_dim, bf16, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? CRA_OK : fail(CRA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
 }
 

@@ -21,6 +21,9 @@
 //               updates the running max / sum and writes P (bf16 / f16,
 //               swizzled) to shared memory.  O is rescaled in TMEM only when
 //               the running max grows by more than 2^8 (exact either way).
+// A CTA may also work on one GPU's shard of a sequence split across GPUs:
+// queries [q_begin, q_begin + q_len) with K / V rows from kv_begin (a W - 1
+// row halo before the shard) and the full global-row list.
 // While one softmax warpgroup works on its scores the tensor core computes
 // the other tile's scores and the PV products (ping-pong).
 #include "geom.cuh"
@@ -62,12 +65,13 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_pairs = (p.S + 2 * kTile - 1) / (2 * kTile);
+  const int n_pairs = (p.q_len + 2 * kTile - 1) / (2 * kTile);
   const int pr = n_pairs - 1 - static_cast<int>(blockIdx.x);  // longest pairs first
   const int h = blockIdx.y, b = blockIdx.z, hk = h / p.kv_groups;
-  const int m0 = pr * 2 * kTile;
-  const int W = p.W, S = p.S, R = p.R;
-  const PairSchedule sch(m0, S, W, R);
+  const int m0 = p.q_begin + pr * 2 * kTile;  // absolute position of the first query
+  const int W = p.W, R = p.R;
+  const int q_end = p.q_begin + p.q_len;
+  const PairSchedule sch(m0, q_end, W, R);
 
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + C::OFF_BAR;
@@ -112,7 +116,7 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
       for (int x = 0; x < nq; ++x)
         for (int c = 0; c < D / 64; ++c)
           tma_load_4d(sbase + C::OFF_Q + x * C::TB + c * kTile * 128, &p.tm_q, BAR(C::B_QFULL), c * 64,
-                      m0 + x * kTile, h, b);
+                      m0 + x * kTile - p.q_begin, h, b);
       int issued = 0;
       for (int i = 0; i < nload; ++i) {
         const int sl = i % C::NSLOT;
@@ -124,8 +128,8 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
         const CUtensorMap* m = g ? (is_v ? &p.tm_gv : &p.tm_gk) : (is_v ? &p.tm_v : &p.tm_k);
         mbar_expect_tx(BAR(C::B_FULL + sl), C::TB);
         for (int c = 0; c < D / 64; ++c)
-          tma_load_4d(sbase + C::OFF_RING + sl * C::TB + c * kTile * 128, m, BAR(C::B_FULL + sl), c * 64, row0, hk,
-                      b);
+          tma_load_4d(sbase + C::OFF_RING + sl * C::TB + c * kTile * 128, m, BAR(C::B_FULL + sl), c * 64,
+                      g ? row0 : row0 - p.kv_begin, hk, b);
         ++issued;
       }
       // Do not leave while copies into this CTA's shared memory are in
@@ -206,7 +210,7 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
     const int r = ((warp & 3) << 5) | lane;  // row = TMEM lane
     const int qi = m0 + x * kTile + r;
     const bool tile_ok = (x == 0) || sch.valid_b;
-    const bool row_ok = qi < S;
+    const bool row_ok = qi < q_end;
     const int ls = local_start(qi, W);
     const int cnt = gcount(qi, W, R);
     const uint32_t lane_off = static_cast<uint32_t>(r & ~31) << 16;
@@ -311,7 +315,7 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
       tc_fence_after();
       const float inv = 1.f / fmaxf(l_run, 1e-6f);
       typename E::T* orow = reinterpret_cast<typename E::T*>(p.out) + b * p.out_sb + h * p.out_sh +
-                            static_cast<int64_t>(qi) * p.out_ss;
+                            static_cast<int64_t>(qi - p.q_begin) * p.out_ss;
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         float o[32];
@@ -330,7 +334,7 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
         }
       }
       if (row_ok)
-        p.lse[(static_cast<int64_t>(b) * p.H + h) * S + qi] =
+        p.lse[(static_cast<int64_t>(b) * p.H + h) * p.q_len + (qi - p.q_begin)] =
             (m_run + log2f(fmaxf(l_run, 1e-6f))) * 0.69314718055994531f;
     }
   }
@@ -347,7 +351,7 @@ static cudaError_t launch_fwd_t(const QueryPassParams& p, cudaStream_t stream) {
   auto kern = fwd_kernel<D, BF16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
-  dim3 grid((p.S + 2 * kTile - 1) / (2 * kTile), p.H, p.B);
+  dim3 grid((p.q_len + 2 * kTile - 1) / (2 * kTile), p.H, p.B);
   kern<<<grid, 320, C::SMEM, stream>>>(p);
   return cudaGetLastError();
 }

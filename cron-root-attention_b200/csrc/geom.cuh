@@ -75,11 +75,13 @@ __host__ __device__ __forceinline__ int first_query_seeing(int g, int S, int W, 
 // [m0 + 128 - 128 t, m0 + 256 - 128 t) -- t = 0 is B's diagonal, t = 1 A's --
 // down to A's lowest local key (without a valid B, the list starts at t = 1).  Global tile g (after the band) covers global
 // rows [128 g, 128 g + 128).  use_a / use_b say which query tile needs the key
-// tile; every listed tile is needed by at least one of them.
+// tile; every listed tile is needed by at least one of them.  Queries at or
+// after q_end (the sequence end, or the end of this GPU's shard) are absent.
 struct PairSchedule {
   int m0, t0, nband, ntiles, lb, ca, cb;
   bool valid_b;
-  __host__ __device__ __forceinline__ PairSchedule(int m0_, int S, int W, int R) : m0(m0_) {
+  __host__ __device__ __forceinline__ PairSchedule(int m0_, int q_end, int W, int R) : m0(m0_) {
+    const int S = q_end;
     valid_b = m0 + kTile < S;
     const int la = local_start(m0, W);
     lb = local_start(m0 + kTile, W);

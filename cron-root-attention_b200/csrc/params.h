@@ -20,6 +20,10 @@ struct alignas(64) QueryPassParams {
   float* lse;         // [B, H, S] fp32, natural log (written by fwd, read by bwd)
   const float* delta; // [B, H, S] fp32, rowsum(O * dO) (backward only)
   int B, H, kv_groups, S, W, R, NG, n_qtiles;
+  // Sequence shard (forward): Q / O / lse rows hold absolute positions
+  // [q_begin, q_begin + q_len); K / V rows start at absolute position
+  // kv_begin.  Whole sequence: q_begin = kv_begin = 0, q_len = S.
+  int q_begin, q_len, kv_begin;
   float scale;        // softmax scale
   float scale_log2;   // softmax scale * log2(e)
   int* err;           // device error word, may be null

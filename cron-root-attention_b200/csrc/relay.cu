@@ -12,6 +12,10 @@
 //     `relay_k * exp(a).to(dtype)`);
 //   * the source positions are written as int32 (the reference stores them
 //     as float32, exact below 2^24, core.py:2807).
+// Rows are indexed locally (0 .. S-1 of the given k / v); pos0 is the
+// absolute sequence position of local row 0 (non-zero for one GPU's shard of
+// a sequence split across GPUs, always a multiple of W), added to the
+// written source positions.
 // Here each W-block is also given its strided row k[r*W] (the phase-2 key,
 // core.py:1042-1087) so that the attention kernels see one prefix-visible
 // list (geom.cuh).
@@ -35,7 +39,7 @@ template <int D, bool BF16>
 __global__ void __launch_bounds__(128) relay_build_kernel(const void* __restrict__ kp, const void* __restrict__ vp,
                                                           int64_t k_sb, int64_t k_sh, int64_t k_ss, int64_t v_sb,
                                                           int64_t v_sh, int64_t v_ss, int Hkv, int S, int W, int NB,
-                                                          int top_k, int R, const float* __restrict__ log_scale,
+                                                          int top_k, int R, int pos0, const float* __restrict__ log_scale,
                                                           void* __restrict__ gkp, void* __restrict__ gvp,
                                                           int32_t* __restrict__ gsrc) {
   using E = Elt<BF16>;
@@ -151,20 +155,20 @@ __global__ void __launch_bounds__(128) relay_build_kernel(const void* __restrict
       *reinterpret_cast<uint4*>(gk + t * D + part * 8) = uk;
       *reinterpret_cast<uint4*>(gv + t * D + part * 8) = uv;
       if (t > 0 && part == 0 && gsrc)
-        gsrc[((static_cast<int64_t>(b) * Hkv + h) * NB + r) * top_k + (t - 1)] = src;
+        gsrc[((static_cast<int64_t>(b) * Hkv + h) * NB + r) * top_k + (t - 1)] = src + pos0;
     }
   }
 }
 
 // host-side launcher (called from capi.cu)
 cudaError_t launch_relay_build(int D, bool bf16, const void* k, const void* v, const int64_t* ks, const int64_t* vs,
-                               int B, int Hkv, int S, int W, int top_k, int R, const float* log_scale, void* gk,
-                               void* gv, int32_t* gsrc, cudaStream_t stream) {
+                               int B, int Hkv, int S, int W, int top_k, int R, int pos0, const float* log_scale,
+                               void* gk, void* gv, int32_t* gsrc, cudaStream_t stream) {
   const int NB = (S + W - 1) / W;
   dim3 grid((NB + 3) / 4, Hkv, B);
 #define CRA_RELAY(DD, BB)                                                                                          \
   relay_build_kernel<DD, BB><<<grid, 128, 0, stream>>>(k, v, ks[0], ks[1], ks[2], vs[0], vs[1], vs[2], Hkv, S, W, \
-                                                       NB, top_k, R, log_scale, gk, gv, gsrc)
+                                                       NB, top_k, R, pos0, log_scale, gk, gv, gsrc)
   if (D == 128) {
     if (bf16) CRA_RELAY(128, true); else CRA_RELAY(128, false);
   } else {

@@ -94,6 +94,34 @@ int cra_fwd(const void* q, const void* k, const void* v, const void* g_k, const 
             int head_dim, int dtype, int use_relay, int top_k, float softmax_scale, void* o, const int64_t* o_strides,
             float* lse, int* dev_error, void* stream);
 
+/* Sequence split across GPUs.  One GPU's shard of a single long sequence
+ * owns the W-block-aligned query range [q_begin, q_begin + q_len) of a
+ * sequence of seq_len tokens.
+ *
+ * cra_relay_build_shard: G rows of the blocks inside rows [row_begin,
+ * row_begin + rows) (row_begin a multiple of W = cra_window(seq_len); only
+ * the sequence's last shard may end inside a block), from this GPU's k / v
+ * rows (local row 0 = absolute position row_begin).  g_k / g_v receive
+ * [batch, kv_heads, nblocks_local * R, head_dim]; g_src absolute positions.
+ * The full list is the concatenation over shards in order (an all-gather).
+ *
+ * cra_fwd_shard: forward for the shard's queries.  q / o / lse hold q_len
+ * rows (lse contiguous [batch, heads, q_len]); k / v hold kv_len rows
+ * starting at absolute position kv_begin <= max(q_begin - (W - 1), 0) (the
+ * local-window halo from the previous shard); g_k / g_v are the FULL global
+ * list of the sequence.  Same numerics as cra_fwd on the whole sequence.
+ * Replaces nothing in the reference (single-GPU only there); used for the
+ * sequence-split configuration. */
+int cra_relay_build_shard(const void* k, const void* v, const int64_t* k_strides, const int64_t* v_strides,
+                          int batch, int kv_heads, int64_t seq_len, int64_t row_begin, int rows, int head_dim,
+                          int dtype, int use_relay, int top_k, const float* relay_log_scale, void* g_k, void* g_v,
+                          int32_t* g_src, void* stream);
+int cra_fwd_shard(const void* q, const void* k, const void* v, const void* g_k, const void* g_v,
+                  const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, int batch, int heads,
+                  int kv_heads, int64_t seq_len, int64_t q_begin, int q_len, int64_t kv_begin, int kv_len,
+                  int head_dim, int dtype, int use_relay, int top_k, float softmax_scale, void* o,
+                  const int64_t* o_strides, float* lse, int* dev_error, void* stream);
+
 /* Bytes of device workspace cra_bwd needs for these sizes (256-byte aligned
  * base required). */
 size_t cra_bwd_workspace_bytes(int batch, int heads, int kv_heads, int seq_len, int head_dim, int use_relay,

@@ -1,0 +1,73 @@
+"""Multi-rank host logic (gloo on CPU, world size 2 and 3): head/batch
+sharding and the sequence split's exchange steps (global-row all-gather and
+halo exchange) checked against the oracle on the whole sequence."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from cron_root_attention.parallel import seq_shard, shard_units, window
+
+
+@pytest.mark.parametrize("B,H,world", [(1, 32, 8), (2, 16, 4), (1, 12, 5), (3, 7, 4), (1, 16, 1)])
+def test_shard_units_partition(B, H, world):
+    seen = []
+    for r in range(world):
+        for b, h0, h1 in shard_units(B, H, world, r):
+            seen += [(b, h) for h in range(h0, h1)]
+    assert sorted(seen) == [(b, h) for b in range(B) for h in range(H)]
+
+
+@pytest.mark.parametrize("S,world", [(524288, 8), (65536, 2), (3000, 3), (2049, 2)])
+def test_seq_shard_block_aligned_cover(S, world):
+    W = window(S)
+    prev = 0
+    for r in range(world):
+        b, e = seq_shard(S, world, r)
+        assert b == prev and b % W == 0 and e > b
+        prev = e
+    assert prev == S
+    if S == 524288:
+        assert W == 725 and {seq_shard(S, 8, r)[1] - seq_shard(S, 8, r)[0] for r in range(7)} <= {90 * 725, 91 * 725}
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, S, out_dir, use_scale):
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    for p in (root, os.path.join(root, "cron-root-attention_b200"), here):
+        sys.path.insert(0, p)
+    import torch.distributed as dist
+    from cron_root_attention.parallel import seq_parallel_forward, seq_shard
+    from shard_oracle import OracleShardOps
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    g = torch.Generator().manual_seed(7)
+    q, k, v = (torch.randn(1, 2, S, 16, generator=g, dtype=torch.float64) for _ in range(3))
+    b, e = seq_shard(S, world, rank)
+    o = seq_parallel_forward(q[:, :, b:e], k[:, :, b:e], v[:, :, b:e], S, ops=OracleShardOps())
+    torch.save(o, os.path.join(out_dir, f"o{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,S", [(2, 3000), (3, 2600), (2, 1500)])
+def test_seq_parallel_forward_gloo(world, S, tmp_path):
+    from oracle import cra_oracle as O
+    mp.spawn(_worker, args=(world, _free_port(), S, str(tmp_path), False), nprocs=world, join=True)
+    o = torch.cat([torch.load(tmp_path / f"o{r}.pt") for r in range(world)], dim=2)
+    g = torch.Generator().manual_seed(7)
+    q, k, v = (torch.randn(1, 2, S, 16, generator=g, dtype=torch.float64) for _ in range(3))
+    ref, _ = O.forward(q, k, v, dtype=torch.float64)
+    assert (o - ref).abs().max().item() < 1e-10

@@ -1,0 +1,85 @@
+"""Sequence split on the GPU: (a) every shard of a 2/3/8-way split run on one
+GPU through the C ABI (cra_relay_build_shard + cra_fwd_shard) with the
+exchange done in-process, against the oracle; (b) the real two-rank NCCL
+path when two GPUs are present."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from oracle import cra_oracle as O
+from parity import fwd_check, inputs
+
+pytestmark = pytest.mark.gpu
+
+
+def _emulate(q, k, v, S, world, dev):
+    from cron_root_attention.parallel import LibcraShardOps, seq_shard, window
+    ops = LibcraShardOps()
+    W = window(S)
+    use_relay = S > 2048
+    gks, gvs, outs = [], [], []
+    bounds = [seq_shard(S, world, r) for r in range(world)]
+    for b, e in bounds:
+        gk, gv = ops.relay_build_shard(k[:, :, b:e].contiguous(), v[:, :, b:e].contiguous(), S, b, use_relay, 2, None)
+        gks.append(gk)
+        gvs.append(gv)
+    gk, gv = torch.cat(gks, 2).contiguous(), torch.cat(gvs, 2).contiguous()
+    for b, e in bounds:
+        kb = max(0, b - (W - 1))
+        outs.append(ops.forward_shard(q[:, :, b:e].contiguous(), k[:, :, kb:e].contiguous(),
+                                      v[:, :, kb:e].contiguous(), gk, gv, S, b, kb, use_relay, 2))
+    torch.cuda.synchronize(dev)
+    return torch.cat(outs, 2)
+
+
+@pytest.mark.parametrize("S,world,D,dt", [(5000, 2, 128, torch.bfloat16), (9000, 3, 64, torch.float16),
+                                          (40000, 8, 128, torch.bfloat16)])
+def test_sequence_split_emulated_on_one_gpu(S, world, D, dt, cuda_device):
+    q, k, v = inputs(1, 2, 2, S, D, dt, 50 + world)
+    o = _emulate(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), S, world, cuda_device)
+    ref, _ = O.forward(q, k, v)
+    r = fwd_check(o, ref, dt)
+    assert r["ok"], r
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _nccl_worker(rank, world, port, S, out):
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    for p in (root, os.path.join(root, "cron-root-attention_b200"), here):
+        sys.path.insert(0, p)
+    import torch.distributed as dist
+    from cron_root_attention.parallel import seq_parallel_forward, seq_shard
+    from parity import inputs
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world)
+    q, k, v = inputs(1, 2, 2, S, 128, torch.bfloat16, 60)
+    b, e = seq_shard(S, world, rank)
+    dev = torch.device("cuda", rank)
+    o = seq_parallel_forward(q[:, :, b:e].to(dev), k[:, :, b:e].to(dev), v[:, :, b:e].to(dev), S)
+    torch.save(o.cpu(), os.path.join(out, f"o{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_sequence_split_nccl_two_ranks(tmp_path):
+    S = 12000
+    mp.spawn(_nccl_worker, args=(2, _port(), S, str(tmp_path)), nprocs=2, join=True)
+    o = torch.cat([torch.load(tmp_path / f"o{r}.pt") for r in range(2)], 2)
+    q, k, v = inputs(1, 2, 2, S, 128, torch.bfloat16, 60)
+    ref, _ = O.forward(q, k, v)
+    r = fwd_check(o, ref, torch.bfloat16)
+    assert r["ok"], r
