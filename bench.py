@@ -309,6 +309,61 @@ def run_ours(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def run_config(args, rank, world, local_rank):
+    """BASELINE configs 4 and 5 (forward only, multi-GPU):
+    c4: B1 H32 D128 S262144 fp16, heads split evenly across ranks, no collective
+        (strong scaling: the total work is fixed);
+    c5: B1 H16 D128 S524288 bf16, one sequence split by W-blocks across ranks,
+        global rows and halo exchanged with NCCL all-gathers (strong scaling)."""
+    import cron_root_attention as cra
+    from cron_root_attention.parallel import seq_parallel_forward, seq_shard, shard_units
+    from oracle import cra_oracle as O
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if args.config == "c4":
+        Bc, Hc, Sc, Dc, dt, seed, sig = 1, 32, 262144, 128, torch.float16, 3, 0.5
+    else:
+        Bc, Hc, Sc, Dc, dt, seed, sig = 1, 16, 524288, 128, torch.bfloat16, 4, 1.0
+    g = torch.Generator().manual_seed(seed)
+    if args.config == "c4":
+        (b, h0, h1), = shard_units(Bc, Hc, world, rank)
+        # each rank draws only its own heads' rows: the same values as slicing the full tensors
+        q, k, v = (torch.randn(Bc, Hc, Sc, Dc, generator=g)[:, h0:h1].mul_(sig).to(dt).to(dev) for _ in range(3))
+        fn = lambda: cra.cron_root_attention(q, k, v)
+    else:
+        s0, s1 = seq_shard(Sc, world, rank)
+        q, k, v = (torch.randn(Bc, Hc, Sc, Dc, generator=g)[:, :, s0:s1].mul_(sig).to(dt).to(dev) for _ in range(3))
+        fn = lambda: seq_parallel_forward(q, k, v, Sc)
+    with torch.no_grad():
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            torch.distributed.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local_rank) as clk:
+            time.sleep(0.6)
+            e0.record()
+            for _ in range(args.steps):
+                fn()
+            e1.record()
+            torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / args.steps
+        if world > 1:
+            t = torch.tensor([ms], device=dev, dtype=torch.float64)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = t.item()
+    f_fwd = 4.0 * Dc * O.visible_pairs(Sc) * Bc * Hc
+    if rank == 0:
+        print(json.dumps({"metric": METRIC, "config": {"workload": args.config, "B": Bc, "H": Hc, "S": Sc, "D": Dc,
+                                                      "dtype": str(dt).replace("torch.", ""),
+                                                      "parallelism": ("heads" if args.config == "c4" else "sequence")
+                                                      + f" split x{world}"},
+                          "value": f_fwd / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms, "n_gpus": world,
+                          "steps": args.steps, "scaling": "strong", "clocks": clk.summary()}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -317,6 +372,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--mode", default="all", choices=["all", "fwd", "fwdbwd"],
                     help="fwd / fwdbwd: time only that pass (for profiling runs)")
+    ap.add_argument("--config", default="northstar", choices=["northstar", "c4", "c5"],
+                    help="c4 / c5: BASELINE configs 4 and 5 (forward, strong scaling over --gpus)")
     ap.add_argument("--heads", type=int, default=H)
     ap.add_argument("--seq", type=int, default=S)
     args = ap.parse_args()
@@ -332,6 +389,8 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
+        elif args.config != "northstar":
+            run_config(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)
     finally:
