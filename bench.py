@@ -269,11 +269,10 @@ def run_ours(args, rank, world, local_rank):
     peaks, peak_src = load_peaks()
     achieved = f_fwd / (ms_kernel * 1e-3) / 1e12
     peak = float(peaks["bf16_tflops"])
-    traffic = None
-    tfile = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tfile):
-        with open(tfile) as f:
-            traffic = json.load(f).get("fwd_kernel_bytes_per_launch")
+    # DRAM bytes per forward launch: ncu dram__bytes_read.sum + write.sum of one
+    # launch at H = 8 (profiles/kernels_northstar_h8.md: 405.9 + 117.1 MB),
+    # scaled by H / 8 (the traffic grows in proportion to the heads)
+    traffic = (405.864704e6 + 117.078272e6) * (H / 8) if (S, D) == (65536, 128) else None
     line = {
         "metric": METRIC,
         "value": world * (f_fwd + f_bwd) / (ms_step * 1e-3) / 1e12,
