@@ -580,8 +580,14 @@ __global__ void __launch_bounds__(320, 1) keypass_kernel(const __grid_constant__
       const int st = u % C::NSQ;
       int h, q0;
       unit(u, h, q0);
-      if (!mbar_wait(BAR(C::B_QFULL + st), (u / C::NSQ) & 1, ab) ||
-          !mbar_wait(BAR(C::B_SFULL + w), (u >> 1) & 1, ab) ||
+      // SFULL first: it implies this unit's Q/dO stage load has completed, and
+      // the stage cannot be refilled before this unit's dV/dK products, so
+      // the QFULL parity test below refers to exactly this load (this
+      // warpgroup skips every other unit, so waiting on QFULL alone could
+      // match an older phase of the stage).  Waiting on QFULL makes the TMA
+      // writes of lse / delta visible to this thread.
+      if (!mbar_wait(BAR(C::B_SFULL + w), (u >> 1) & 1, ab) ||
+          !mbar_wait(BAR(C::B_QFULL + st), (u / C::NSQ) & 1, ab) ||
           (u >= 2 && !mbar_wait(BAR(C::B_PFREE + w), ((u >> 1) - 1) & 1, ab))) {
         ok = false;
         break;

@@ -75,27 +75,25 @@ def test_stride_zero_grad_output(cuda_device):
 
 def test_config3_full_size(cuda_device):
     """B2 H16 D128 S65536 bf16, seed 2, dO ~ N(0,1).
-    Checked through (a) sampled output rows and dQ rows against the oracle
-    (rows at the start, middle and end of one (b, h)) and (b) identities that
-    hold at any size: sum_j dV_j = sum_q dO_q and sum_j dK_j = 0 per (b, h)."""
+    (a) Two whole (b, h) slices -- every row -- of o, dq, dk, dv against the
+    fp32 oracle restatement (the backward restatement is exact for dk / dv
+    only with every query row, hence whole slices); (b) identities that hold
+    at any size over all (b, h): sum_j dV_j = sum_q dO_q, sum_j dK_j = 0."""
     dev = cuda_device
     B, H, S, D = 2, 16, 65536, 128
     q, k, v, do = inputs(B, H, H, S, D, torch.bfloat16, 2, with_do=True)
     o, dq, dk, dv, _ = _grads(q, k, v, do, dev)
     assert not any(torch.isnan(t).any().item() for t in (o, dq, dk, dv))
-    # (b) identities, in fp64 over every (b, h)
     sdv = dv.double().sum(2).cpu()
     sdo = do.double().sum(2)
     assert rel_l2(sdv, sdo) <= GRAD_REL_L2
-    sdk = dk.double().sum(2).cpu()
-    assert (sdk.norm() / dk.double().norm().cpu()).item() <= 1e-2
-    # (a) sampled rows of (b=1, h=5)
-    bh = (slice(1, 2), slice(5, 6))
-    qs, ks, vs, dos = (t[bh] for t in (q, k, v, do))
-    for r0 in (0, 31744, S - 512):
-        rows = (r0, r0 + 512)
-        ro, _ = O.forward(qs, ks, vs, rows=rows)
-        _r = fwd_check(o[bh][:, :, r0:r0 + 512], ro[:, :, r0:r0 + 512], torch.bfloat16)
+    # bf16 rounding of dK alone leaves ~2e-3 of this ratio
+    assert (dk.double().sum(2).cpu().norm() / dk.double().norm().cpu()).item() <= 1e-2
+    torch.set_num_threads(max(1, torch.get_num_threads()))
+    for b, h in ((1, 5), (0, 15)):
+        sl = lambda t: t[b:b + 1, h:h + 1]
+        ro, rdq, rdk, rdv, _ = O.forward_backward(sl(q), sl(k), sl(v), sl(do), dtype=torch.float32)
+        _r = fwd_check(sl(o), ro, torch.bfloat16)
         assert _r["ok"], _r
-        _, rdq, _, _, _ = O.forward_backward(qs, ks, vs, dos, rows=rows)
-        assert rel_l2(dq[bh][:, :, r0:r0 + 512], rdq[:, :, r0:r0 + 512]) <= GRAD_REL_L2
+        for name, x, y in (("dq", sl(dq), rdq), ("dk", sl(dk), rdk), ("dv", sl(dv), rdv)):
+            assert rel_l2(x, y) <= GRAD_REL_L2, (name, rel_l2(x, y))

@@ -63,6 +63,19 @@ def test_forward_vs_oracle(B, H, S, D, dt, seed, sigma, cuda_device):
     assert r["ok"], r
 
 
+def test_northstar_forward_every_row(cuda_device):
+    """North-star shape (B1 H16 D128 S65536 bf16): two whole heads checked
+    row by row against the oracle, three calls in a row (a race that corrupts
+    one query tile now and then would show here)."""
+    q, k, v = inputs(1, 16, 16, 65536, 128, torch.bfloat16, 2)
+    for _ in range(3):
+        o = _run(q, k, v, cuda_device)
+        for h in (0, 11):
+            ref, _ = O.forward(q[:, h:h + 1], k[:, h:h + 1], v[:, h:h + 1])
+            r = fwd_check(o[:, h:h + 1], ref, torch.bfloat16)
+            assert r["ok"], r
+
+
 def test_config2_full_size(cuda_device):
     """B1 H12 D64 S16384 fp16, N(0,1)*0.5, seed 1."""
     q, k, v = inputs(1, 12, 12, 16384, 64, torch.float16, 1, 0.5)
