@@ -383,28 +383,30 @@ __global__ void __launch_bounds__(320, 1) dq_kernel(const __grid_constant__ Quer
 // (K/V rows in LOCAL mode, global rows G in GLOBAL mode).  The queries that
 // see the tile are walked in 64-query units; per unit:
 //   S^T = K Q_u^T, dP^T = V dO_u^T  (one of two TMEM slots),
-//   P^T, dS^T -> shared memory (per slot),
-//   dV += P^T dO_u,  dK += dS^T Q_u  (TMEM accumulators).
-// The two softmax warpgroups take alternate units.
+//   P^T, dS^T (16-bit) written back into the same TMEM slot,
+//   dV += P^T dO_u,  dK += dS^T Q_u  (TMEM accumulators; A operands read
+//   from TMEM, so only dO_u / Q_u come from shared memory).
+// The two softmax warpgroups take alternate units.  A slot is reused only
+// after the dV / dK products that read it have completed (GDONE).
 // ===========================================================================
 template <int D>
 struct KeyCfg {
   static constexpr int TB = kTile * D * 2;         // K or V tile
   static constexpr int UB = kUnit * D * 2;         // Q or dO unit
-  static constexpr int NSQ = (D == 128) ? 3 : 6;   // Q/dO unit stages
-  static constexpr int PB = kTile * kUnit * 2;     // P^T (or dS^T) per slot
+  static constexpr int NSQ = (D == 128) ? 4 : 8;   // Q/dO unit stages
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + TB;
   static constexpr int OFF_Q = OFF_V + TB;         // stage s: Q at OFF_Q + 2 s UB, dO after it
-  static constexpr int OFF_PT = OFF_Q + NSQ * 2 * UB;  // slot s: P^T at OFF_PT + 2 s PB, dS^T after it
-  static constexpr int OFF_LSE = OFF_PT + 4 * PB;  // stage s: lse2[64], delta[64]
+  static constexpr int OFF_LSE = OFF_Q + NSQ * 2 * UB;  // stage s: lse2[64], delta[64]
   static constexpr int OFF_BAR = OFF_LSE + NSQ * 2 * kUnit * 4;
-  static constexpr int B_KVFULL = 0, B_QFULL = 1, B_QEMPTY = 1 + NSQ, B_SFULL = 1 + 2 * NSQ, B_SFREE = B_SFULL + 2,
-                       B_PFULL = B_SFREE + 2, B_PFREE = B_PFULL + 2, B_DONE = B_PFREE + 2, B_DRAIN = B_DONE + 1,
-                       N_BAR = B_DRAIN + 1;
+  static constexpr int B_KVFULL = 0, B_QFULL = 1, B_QEMPTY = 1 + NSQ, B_SFULL = 1 + 2 * NSQ, B_PFULL = B_SFULL + 2,
+                       B_GDONE = B_PFULL + 2, B_DONE = B_GDONE + 2, B_DRAIN = B_DONE + 1, N_BAR = B_DRAIN + 1;
   static constexpr int OFF_MISC = OFF_BAR + N_BAR * 8;
   static constexpr int SMEM = OFF_MISC + 16 + 1024;
-  // TMEM: slot s -> S^T at 128 s, dP^T at 128 s + 64; dV at 256, dK at 256 + D
+  // TMEM: slot s -> S^T at 128 s, dP^T at 128 s + 64 (fp32, 64 columns each);
+  // the softmax overwrites them with P^T (128 s, 32 columns of 16-bit pairs)
+  // and dS^T (128 s + 64), which the dV / dK products read from TMEM.
+  // dV at 256, dK at 256 + D.
   static constexpr int COL_DV = 256, COL_DK = 256 + D;
   static_assert(SMEM <= 232448, "shared memory budget");
 };
@@ -457,9 +459,8 @@ __global__ void __launch_bounds__(320, 1) keypass_kernel(const __grid_constant__
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(BAR(C::B_SFULL + s), 1);
-      mbar_init(BAR(C::B_SFREE + s), 128);
       mbar_init(BAR(C::B_PFULL + s), 128);
-      mbar_init(BAR(C::B_PFREE + s), 1);
+      mbar_init(BAR(C::B_GDONE + s), 1);
     }
     mbar_init(BAR(C::B_DONE), 1);
     mbar_init(BAR(C::B_DRAIN), 1);
@@ -518,23 +519,23 @@ __global__ void __launch_bounds__(320, 1) keypass_kernel(const __grid_constant__
         if (!mbar_wait(BAR(C::B_PFULL + sl), (i >> 1) & 1, ab)) return false;
         tc_fence_after();
         const uint32_t qd = sbase + C::OFF_Q + st * 2 * C::UB;
-        const uint32_t pts = sbase + C::OFF_PT + sl * 2 * C::PB, dsts = pts + C::PB;
 #pragma unroll
         for (int kk = 0; kk < kUnit / 16; ++kk) {
           const uint32_t boff = kk * 16 * 128;
-          mma_ss(tmem + C::COL_DV, sdesc(pts + kk * 32, 16, 1024), sdesc(qd + C::UB + boff, kUnit * 128, 1024), ID_G,
+          mma_ts(tmem + C::COL_DV, tmem + 128 * sl + kk * 8, sdesc(qd + C::UB + boff, kUnit * 128, 1024), ID_G,
                  (i > 0 || kk > 0) ? 1u : 0u);
-          mma_ss(tmem + C::COL_DK, sdesc(dsts + kk * 32, 16, 1024), sdesc(qd + boff, kUnit * 128, 1024), ID_G,
+          mma_ts(tmem + C::COL_DK, tmem + 128 * sl + 64 + kk * 8, sdesc(qd + boff, kUnit * 128, 1024), ID_G,
                  (i > 0 || kk > 0) ? 1u : 0u);
         }
-        mma_commit(BAR(C::B_PFREE + sl));
+        mma_commit(BAR(C::B_GDONE + sl));
         mma_commit(BAR(C::B_QEMPTY + st));
         return true;
       };
       for (int u = 0; ok && u < nU; ++u) {
         const int st = u % C::NSQ, sl = u & 1;
+        // slot sl was last read by the dV / dK products of unit u - 2
         if (!mbar_wait(BAR(C::B_QFULL + st), (u / C::NSQ) & 1, ab) ||
-            (u >= 2 && !mbar_wait(BAR(C::B_SFREE + sl), ((u >> 1) - 1) & 1, ab))) {
+            (u >= 2 && !mbar_wait(BAR(C::B_GDONE + sl), ((u >> 1) - 1) & 1, ab))) {
           ok = false;
           break;
         }
@@ -574,7 +575,7 @@ __global__ void __launch_bounds__(320, 1) keypass_kernel(const __grid_constant__
       qa = kj;
       qb = kj < S ? min(kj + W, S) : kj;
     }
-    uint8_t* ptrow = smem + C::OFF_PT + w * 2 * C::PB + r * 128;
+    const uint32_t scol = tmem + lane_off + 128 * w;
     bool ok = true;
     for (int u = w; u < nU; u += 2) {
       const int st = u % C::NSQ;
@@ -587,8 +588,7 @@ __global__ void __launch_bounds__(320, 1) keypass_kernel(const __grid_constant__
       // match an older phase of the stage).  Waiting on QFULL makes the TMA
       // writes of lse / delta visible to this thread.
       if (!mbar_wait(BAR(C::B_SFULL + w), (u >> 1) & 1, ab) ||
-          !mbar_wait(BAR(C::B_QFULL + st), (u / C::NSQ) & 1, ab) ||
-          (u >= 2 && !mbar_wait(BAR(C::B_PFREE + w), ((u >> 1) - 1) & 1, ab))) {
+          !mbar_wait(BAR(C::B_QFULL + st), (u / C::NSQ) & 1, ab)) {
         ok = false;
         break;
       }
@@ -599,8 +599,8 @@ __global__ void __launch_bounds__(320, 1) keypass_kernel(const __grid_constant__
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         float s[32], dp[32];
-        tmem_ld32(tmem + lane_off + 128 * w + 32 * c, s);
-        tmem_ld32(tmem + lane_off + 128 * w + 64 + 32 * c, dp);
+        tmem_ld32(scol + 32 * c, s);
+        tmem_ld32(scol + 64 + 32 * c, dp);
         tmem_ld_wait();
         uint32_t ppk[16], dpk[16];
 #pragma unroll
@@ -611,17 +611,13 @@ __global__ void __launch_bounds__(320, 1) keypass_kernel(const __grid_constant__
           ppk[e / 2] = E::pack(p0, p1);
           dpk[e / 2] = E::pack(p0 * (dp[e] - sm_di[col]), p1 * (dp[e + 1] - sm_di[col + 1]));
         }
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint32_t off = ((4 * c + q) ^ (r & 7)) << 4;
-          *reinterpret_cast<uint4*>(ptrow + off) = make_uint4(ppk[4 * q], ppk[4 * q + 1], ppk[4 * q + 2], ppk[4 * q + 3]);
-          *reinterpret_cast<uint4*>(ptrow + C::PB + off) =
-              make_uint4(dpk[4 * q], dpk[4 * q + 1], dpk[4 * q + 2], dpk[4 * q + 3]);
-        }
+        // chunk c of P^T / dS^T overwrites score columns [16c, 16c+16) of
+        // S^T / dP^T, already consumed (columns [0, 32c+32) have been read)
+        tmem_st16(scol + 16 * c, ppk);
+        tmem_st16(scol + 64 + 16 * c, dpk);
       }
+      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(BAR(C::B_SFREE + w));
-      fence_proxy_async_smem();
       mbar_arrive(BAR(C::B_PFULL + w));
     }
     // ------------------------------------------------------------ epilogue
