@@ -18,8 +18,7 @@
 //   keypass<LOCAL>   one CTA per 128-key tile: dK / dV over the local band,
 //                    then folds in dG of the tile's strided key and of every
 //                    relay row whose source lies in the tile, and stores.
-//   dq_kernel        one CTA per pair of 128-query tiles: dQ over band + global
-//                    prefix.
+//   dq_kernel        one CTA per 128-query tile: dQ over band + global prefix.
 // The result is deterministic: every sum has a fixed order.
 //
 // The attention kernels use the warp roles of the forward (fwd.cu): warp 0
@@ -75,57 +74,53 @@ __global__ void __launch_bounds__(256) delta_kernel(const void* __restrict__ op,
 }
 
 // ===========================================================================
-// dQ: query-centric.  A CTA owns TWO 128-query tiles (A = [m0, m0+128),
-// B = [m0+128, m0+256)) and streams the keys they need (PairSchedule: local
-// band, then global prefix) once, in 64-key units; halves no row needs are
-// skipped.  Per unit and query tile x: S_x = Q_x K_u^T and dP_x = dO_x V_u^T
-// into x's TMEM slot, dS_x = P * (dP - Di) (P from the stored lse) -> shared
-// memory, dQ_x += dS_x K_u.  Softmax warpgroup x serves query tile x; while
-// one works, the tensor core computes the other tile's products (ping-pong),
-// and K/V are read from L2 once per 256 queries.
+// dQ: query-centric.  A CTA owns one 128-query tile and walks the forward's
+// key tiles (band, then global prefix) in 64-key units, skipping halves no row
+// needs.  Per unit: S = Q K_u^T and dP = dO V_u^T into one of two TMEM slots;
+// the softmax writes dS = P * (dP - Di) (P from the stored lse, 16-bit) back
+// into the slot; dQ += dS K_u reads dS from TMEM (TS-form MMA), so only K_u
+// comes from shared memory.  The two softmax warpgroups take alternate units
+// (the backward softmax has no running state).  A slot is reused once the dQ
+// product that read it has completed.
 // ===========================================================================
 struct DqUnits {
-  PairSchedule ps;
-  int la, qa_max, qb_max;
-  __device__ __forceinline__ DqUnits(int m0, int S, int W, int R) : ps(m0, S, W, R) {
-    la = local_start(m0, W);
-    qa_max = min(m0 + kTile - 1, S - 1);
-    qb_max = min(m0 + 2 * kTile - 1, S - 1);
+  int m0, nband, ntiles, ls0, qmax, cmax;
+  __device__ __forceinline__ DqUnits(int m0_, int S, int W, int R) : m0(m0_) {
+    nband = band_tiles(m0, W);
+    ntiles = nband + global_tiles(m0, S, W, R);
+    ls0 = local_start(m0, W);
+    qmax = min(m0 + kTile - 1, S - 1);
+    cmax = gcount(qmax, W, R);
   }
-  // half hh of schedule tile j: first key / global row, which query tiles
-  // need it; false when neither does
-  __device__ __forceinline__ bool get(int j, int hh, int& row0, bool& g, bool& ua, bool& ub) const {
-    bool ta, tb;
-    ps.tile(j, row0, g, ta, tb);
-    row0 += kUnit * hh;
-    if (!g) {
-      ua = ta && row0 <= qa_max && row0 + kUnit > la;
-      ub = tb && row0 <= qb_max && row0 + kUnit > ps.lb;
-    } else {
-      ua = ta && row0 < ps.ca;
-      ub = tb && row0 < ps.cb;
+  // half hh of key tile j: first key row / global row, and whether any row of
+  // the tile needs it
+  __device__ __forceinline__ bool get(int j, int hh, int& row0, bool& g) const {
+    if (j < nband) {
+      g = false;
+      row0 = m0 - j * kTile + kUnit * hh;
+      return row0 <= qmax && row0 + kUnit > ls0;
     }
-    return ua || ub;
+    g = true;
+    row0 = (j - nband) * kTile + kUnit * hh;
+    return row0 < cmax;
   }
 };
 
 template <int D>
 struct DqCfg {
-  static constexpr int TB = kTile * D * 2;    // one Q or dO tile
-  static constexpr int UB = kUnit * D * 2;    // one K or V unit
-  static constexpr int NSLOT = (D == 128) ? 4 : 8;  // ring of K / V units
-  static constexpr int DSB = kTile * kUnit * 2;     // dS of one query tile
-  static constexpr int OFF_Q = 0;             // Q_A, Q_B
-  static constexpr int OFF_DO = OFF_Q + 2 * TB;     // dO_A, dO_B
-  static constexpr int OFF_RING = OFF_DO + 2 * TB;
-  static constexpr int OFF_DS = OFF_RING + NSLOT * UB;  // dS_A, dS_B
-  static constexpr int OFF_BAR = OFF_DS + 2 * DSB;
-  static constexpr int B_QFULL = 0, B_FULL = 1, B_EMPTY = 1 + NSLOT;
-  static constexpr int B_SFULL = 1 + 2 * NSLOT, B_SFREE = B_SFULL + 2, B_DSFULL = B_SFREE + 2,
-                       B_DSFREE = B_DSFULL + 2, B_DONE = B_DSFREE + 2, B_DRAIN = B_DONE + 1, N_BAR = B_DRAIN + 1;
+  static constexpr int TB = kTile * D * 2;   // Q / dO tile
+  static constexpr int UB = kUnit * D * 2;   // one K or V unit
+  static constexpr int NSLOT = (D == 128) ? 10 : 20;  // ring entries K_0, V_0, K_1, V_1, ...
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_DO = OFF_Q + TB;
+  static constexpr int OFF_RING = OFF_DO + TB;
+  static constexpr int OFF_BAR = OFF_RING + NSLOT * UB;
+  static constexpr int B_QFULL = 0, B_FULL = 1, B_EMPTY = 1 + NSLOT, B_SFULL = 1 + 2 * NSLOT, B_DSFULL = B_SFULL + 2,
+                       B_DQDONE = B_DSFULL + 2, B_DONE = B_DQDONE + 2, B_DRAIN = B_DONE + 1, N_BAR = B_DRAIN + 1;
   static constexpr int OFF_MISC = OFF_BAR + N_BAR * 8;
   static constexpr int SMEM = OFF_MISC + 16 + 1024;
-  // TMEM: tile x -> S at 128 x, dP at 128 x + 64; dQ_x at 256 + x D
+  // TMEM: slot s -> S at 128 s, dP at 128 s + 64 (fp32, 64 columns each; dS
+  // overwrites the first 32 columns of S as 16-bit pairs); dQ at 256
   static constexpr int COL_DQ = 256;
   static_assert(SMEM <= 232448, "shared memory budget");
 };
@@ -137,14 +132,12 @@ __global__ void __launch_bounds__(320, 1) dq_kernel(const __grid_constant__ Quer
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_pairs = (p.S + 2 * kTile - 1) / (2 * kTile);
-  const int pr = n_pairs - 1 - static_cast<int>(blockIdx.x);  // longest pairs first
+  const int qt = p.n_qtiles - 1 - static_cast<int>(blockIdx.x);  // longest tiles first
   const int h = blockIdx.y, b = blockIdx.z, hk = h / p.kv_groups;
-  const int m0 = pr * 2 * kTile;
+  const int m0 = qt * kTile;
   const int W = p.W, S = p.S, R = p.R;
   const int Spad = p.n_qtiles * kTile;
   const DqUnits un(m0, S, W, R);
-  const int ntiles = un.ps.ntiles;
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + C::OFF_BAR;
   auto BAR = [&](int i) { return bar0 + 8u * i; };
@@ -158,11 +151,10 @@ __global__ void __launch_bounds__(320, 1) dq_kernel(const __grid_constant__ Quer
       mbar_init(BAR(C::B_FULL + i), 1);
       mbar_init(BAR(C::B_EMPTY + i), 1);
     }
-    for (int x = 0; x < 2; ++x) {
-      mbar_init(BAR(C::B_SFULL + x), 1);
-      mbar_init(BAR(C::B_SFREE + x), 128);
-      mbar_init(BAR(C::B_DSFULL + x), 128);
-      mbar_init(BAR(C::B_DSFREE + x), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(BAR(C::B_SFULL + s), 1);
+      mbar_init(BAR(C::B_DSFULL + s), 128);
+      mbar_init(BAR(C::B_DQDONE + s), 1);
     }
     mbar_init(BAR(C::B_DONE), 1);
     mbar_init(BAR(C::B_DRAIN), 1);
@@ -177,22 +169,18 @@ __global__ void __launch_bounds__(320, 1) dq_kernel(const __grid_constant__ Quer
 
   if (warp == 0) {
     if (lane == 0) {
-      const int nq = un.ps.valid_b ? 2 : 1;
-      mbar_expect_tx(BAR(C::B_QFULL), 2 * nq * C::TB);
-      for (int x = 0; x < nq; ++x)
-        for (int c = 0; c < D / 64; ++c) {
-          tma_load_4d(sbase + C::OFF_Q + x * C::TB + c * kTile * 128, &p.tm_q, BAR(C::B_QFULL), c * 64,
-                      m0 + x * kTile, h, b);
-          tma_load_4d(sbase + C::OFF_DO + x * C::TB + c * kTile * 128, &p.tm_do, BAR(C::B_QFULL), c * 64,
-                      m0 + x * kTile, h, b);
-        }
-      int e = 0;  // ring entries: K_0, V_0, K_1, V_1, ...
+      mbar_expect_tx(BAR(C::B_QFULL), 2 * C::TB);
+      for (int c = 0; c < D / 64; ++c) {
+        tma_load_4d(sbase + C::OFF_Q + c * kTile * 128, &p.tm_q, BAR(C::B_QFULL), c * 64, m0, h, b);
+        tma_load_4d(sbase + C::OFF_DO + c * kTile * 128, &p.tm_do, BAR(C::B_QFULL), c * 64, m0, h, b);
+      }
+      int e = 0;
       bool ok = true;
-      for (int j = 0; ok && j < ntiles; ++j)
-        for (int hh = 0; hh < 2; ++hh) {
+      for (int j = 0; ok && j < un.ntiles; ++j)
+        for (int hh = 0; hh < 2 && ok; ++hh) {
           int row0;
-          bool g, ua, ub;
-          if (!un.get(j, hh, row0, g, ua, ub)) continue;
+          bool g;
+          if (!un.get(j, hh, row0, g)) continue;
           for (int kv = 0; kv < 2; ++kv, ++e) {
             const int sl = e % C::NSLOT;
             if (e >= C::NSLOT && !mbar_wait(BAR(C::B_EMPTY + sl), ((e / C::NSLOT) - 1) & 1, ab)) { ok = false; break; }
@@ -202,7 +190,6 @@ __global__ void __launch_bounds__(320, 1) dq_kernel(const __grid_constant__ Quer
               tma_load_4d(sbase + C::OFF_RING + sl * C::UB + c * kUnit * 128, m, BAR(C::B_FULL + sl), c * 64, row0,
                           hk, b);
           }
-          if (!ok) break;
         }
       if (*abort_flag)
         for (int i = (e > C::NSLOT ? e - C::NSLOT : 0); i < e; ++i)
@@ -213,68 +200,52 @@ __global__ void __launch_bounds__(320, 1) dq_kernel(const __grid_constant__ Quer
     if (lane == 0) {
       constexpr uint32_t ID_S = idesc_f16(BF16, kTile, kUnit, false, false);
       constexpr uint32_t ID_Q = idesc_f16(BF16, kTile, D, false, true);
+      const uint32_t qs = sbase + C::OFF_Q, dos = sbase + C::OFF_DO;
       bool ok = mbar_wait(BAR(C::B_QFULL), 0, ab);
-      int ns[2] = {0, 0}, nq[2] = {0, 0};
-      // dQ_x += dS_x K for the unit whose K sits in ring entry ek
-      auto issue_dq = [&](int ek, bool ua, bool ub) -> bool {
-        const int sl = ek % C::NSLOT;
-        const uint32_t ks = sbase + C::OFF_RING + sl * C::UB;
-        const bool use[2] = {ua, ub};
-        for (int x = 0; x < 2; ++x) {
-          if (!use[x]) continue;
-          if (!mbar_wait(BAR(C::B_DSFULL + x), nq[x] & 1, ab)) return false;
-          tc_fence_after();
-          const uint32_t dss = sbase + C::OFF_DS + x * C::DSB;
+      // dQ += dS K for unit i (its K sits in ring entry 2 i)
+      auto issue_dq = [&](int i) -> bool {
+        const int sl = i & 1, ek = (2 * i) % C::NSLOT;
+        if (!mbar_wait(BAR(C::B_DSFULL + sl), (i >> 1) & 1, ab)) return false;
+        tc_fence_after();
+        const uint32_t ks = sbase + C::OFF_RING + ek * C::UB;
 #pragma unroll
-          for (int kk = 0; kk < kUnit / 16; ++kk)
-            mma_ss(tmem + C::COL_DQ + x * D, sdesc(dss + kk * 32, 16, 1024),
-                   sdesc(ks + kk * 16 * 128, kUnit * 128, 1024), ID_Q, (nq[x] > 0 || kk > 0) ? 1u : 0u);
-          mma_commit(BAR(C::B_DSFREE + x));
-          ++nq[x];
-        }
-        mma_commit(BAR(C::B_EMPTY + sl));
+        for (int kk = 0; kk < kUnit / 16; ++kk)
+          mma_ts(tmem + C::COL_DQ, tmem + 128 * sl + kk * 8, sdesc(ks + kk * 16 * 128, kUnit * 128, 1024), ID_Q,
+                 (i > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(BAR(C::B_DQDONE + sl));
+        mma_commit(BAR(C::B_EMPTY + ek));
         return true;
       };
-      int e = 0, prev_ek = -1;
-      bool prev_a = false, prev_b = false;
-      for (int j = 0; ok && j < ntiles; ++j)
+      int u = 0;
+      for (int j = 0; ok && j < un.ntiles; ++j)
         for (int hh = 0; ok && hh < 2; ++hh) {
           int row0;
-          bool g, use[2];
-          if (!un.get(j, hh, row0, g, use[0], use[1])) continue;
-          const int ek = e, ev = e + 1;
-          e += 2;
+          bool g;
+          if (!un.get(j, hh, row0, g)) continue;
+          const int sl = u & 1, ek = 2 * u, ev = 2 * u + 1;
           if (!mbar_wait(BAR(C::B_FULL + ek % C::NSLOT), (ek / C::NSLOT) & 1, ab) ||
-              !mbar_wait(BAR(C::B_FULL + ev % C::NSLOT), (ev / C::NSLOT) & 1, ab)) {
+              !mbar_wait(BAR(C::B_FULL + ev % C::NSLOT), (ev / C::NSLOT) & 1, ab) ||
+              (u >= 2 && !mbar_wait(BAR(C::B_DQDONE + sl), ((u >> 1) - 1) & 1, ab))) {
             ok = false;
             break;
           }
+          tc_fence_after();
           const uint32_t ks = sbase + C::OFF_RING + (ek % C::NSLOT) * C::UB;
           const uint32_t vs = sbase + C::OFF_RING + (ev % C::NSLOT) * C::UB;
-          for (int x = 0; x < 2; ++x) {
-            if (!use[x]) continue;
-            if (ns[x] > 0 && !mbar_wait(BAR(C::B_SFREE + x), (ns[x] - 1) & 1, ab)) { ok = false; break; }
-            tc_fence_after();
-            const uint32_t qs = sbase + C::OFF_Q + x * C::TB, dos = sbase + C::OFF_DO + x * C::TB;
 #pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk) {
-              const uint32_t qo = (kk >> 2) * kTile * 128 + (kk & 3) * 32;
-              const uint32_t ko = (kk >> 2) * kUnit * 128 + (kk & 3) * 32;
-              mma_ss(tmem + 128 * x, sdesc(qs + qo, 16, 1024), sdesc(ks + ko, 16, 1024), ID_S, kk > 0 ? 1u : 0u);
-              mma_ss(tmem + 128 * x + 64, sdesc(dos + qo, 16, 1024), sdesc(vs + ko, 16, 1024), ID_S,
-                     kk > 0 ? 1u : 0u);
-            }
-            mma_commit(BAR(C::B_SFULL + x));
-            ++ns[x];
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t qo = (kk >> 2) * kTile * 128 + (kk & 3) * 32;
+            const uint32_t ko = (kk >> 2) * kUnit * 128 + (kk & 3) * 32;
+            mma_ss(tmem + 128 * sl, sdesc(qs + qo, 16, 1024), sdesc(ks + ko, 16, 1024), ID_S, kk > 0 ? 1u : 0u);
+            mma_ss(tmem + 128 * sl + 64, sdesc(dos + qo, 16, 1024), sdesc(vs + ko, 16, 1024), ID_S,
+                   kk > 0 ? 1u : 0u);
           }
-          if (!ok) break;
+          mma_commit(BAR(C::B_SFULL + sl));
           mma_commit(BAR(C::B_EMPTY + ev % C::NSLOT));  // V_u is no longer needed
-          if (prev_ek >= 0 && !issue_dq(prev_ek, prev_a, prev_b)) { ok = false; break; }
-          prev_ek = ek;
-          prev_a = use[0];
-          prev_b = use[1];
+          if (u > 0 && !issue_dq(u - 1)) { ok = false; break; }
+          ++u;
         }
-      if (ok && prev_ek >= 0) ok = issue_dq(prev_ek, prev_a, prev_b);
+      if (ok && u > 0) ok = issue_dq(u - 1);
       if (ok) mma_commit(BAR(C::B_DONE));
       if (!ok) {
         mma_commit(BAR(C::B_DRAIN));
@@ -283,28 +254,28 @@ __global__ void __launch_bounds__(320, 1) dq_kernel(const __grid_constant__ Quer
     }
     __syncwarp();
   } else {
-    const int x = (warp - 2) >> 2;           // query tile served by this warpgroup
+    const int w = (warp - 2) >> 2;           // softmax warpgroup: units with (u & 1) == w
     const int r = ((warp & 3) << 5) | lane;  // query row = TMEM lane
-    const int qi = m0 + x * kTile + r;
-    const bool tile_ok = x == 0 || un.ps.valid_b;
+    const int qi = m0 + r;
     const bool row_ok = qi < S;
     const int ls = local_start(qi, W);
     const int cnt = gcount(qi, W, R);
     const uint32_t lane_off = static_cast<uint32_t>(r & ~31) << 16;
+    const uint32_t scol = tmem + lane_off + 128 * w;
     const float sl2 = p.scale_log2;
-    const int64_t rowi = (static_cast<int64_t>(b) * p.H + h) * Spad + min(qi, Spad - 1);
+    const int64_t rowi = (static_cast<int64_t>(b) * p.H + h) * Spad + qi;
     const float lse2 = p.lse[rowi];  // lse * log2(e), padded array
     const float di = p.delta[rowi];
-    uint8_t* dsrow = smem + C::OFF_DS + x * C::DSB + r * 128;
     bool ok = true;
-    int n = 0;
-    for (int j = 0; ok && tile_ok && j < ntiles; ++j)
+    int u = 0;
+    for (int j = 0; ok && j < un.ntiles; ++j)
       for (int hh = 0; hh < 2; ++hh) {
         int row0;
-        bool g, use[2];
-        if (!un.get(j, hh, row0, g, use[0], use[1]) || !use[x]) continue;
-        if (!mbar_wait(BAR(C::B_SFULL + x), n & 1, ab) ||
-            (n > 0 && !mbar_wait(BAR(C::B_DSFREE + x), (n - 1) & 1, ab))) {
+        bool g;
+        if (!un.get(j, hh, row0, g)) continue;
+        const int uu = u++;
+        if ((uu & 1) != w) continue;
+        if (!mbar_wait(BAR(C::B_SFULL + w), (uu >> 1) & 1, ab)) {
           ok = false;
           break;
         }
@@ -321,8 +292,8 @@ __global__ void __launch_bounds__(320, 1) dq_kernel(const __grid_constant__ Quer
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           float s[32], dp[32];
-          tmem_ld32(tmem + lane_off + 128 * x + 32 * c, s);
-          tmem_ld32(tmem + lane_off + 128 * x + 64 + 32 * c, dp);
+          tmem_ld32(scol + 32 * c, s);
+          tmem_ld32(scol + 64 + 32 * c, dp);
           tmem_ld_wait();
           uint32_t pk[16];
 #pragma unroll
@@ -332,27 +303,23 @@ __global__ void __launch_bounds__(320, 1) dq_kernel(const __grid_constant__ Quer
             const float p1 = (col + 1 >= lo && col + 1 < hi) ? ex2(fmaf(s[e2 + 1], sl2, -lse2)) : 0.f;
             pk[e2 / 2] = E::pack(p0 * (dp[e2] - di), p1 * (dp[e2 + 1] - di));
           }
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            *reinterpret_cast<uint4*>(dsrow + (((4 * c + q) ^ (r & 7)) << 4)) =
-                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          // chunk c of dS overwrites S columns [16c, 16c+16), already read
+          tmem_st16(scol + 16 * c, pk);
         }
+        tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(BAR(C::B_SFREE + x));
-        fence_proxy_async_smem();
-        mbar_arrive(BAR(C::B_DSFULL + x));
-        ++n;
+        mbar_arrive(BAR(C::B_DSFULL + w));
       }
-    // epilogue: warpgroup x writes dQ of query tile x
-    if (tile_ok && ok && (n == 0 || mbar_wait(BAR(C::B_DONE), 0, ab))) {
+    // epilogue: warpgroup w writes columns [w * D/2, (w+1) * D/2) of dQ
+    if (ok && (u == 0 || mbar_wait(BAR(C::B_DONE), 0, ab))) {
       tc_fence_after();
       typename E::T* orow = reinterpret_cast<typename E::T*>(p.out) + b * p.out_sb + h * p.out_sh +
                             static_cast<int64_t>(qi) * p.out_ss;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = w * (D / 64); c < (w + 1) * (D / 64); ++c) {
         float o[32];
-        if (n > 0) {
-          tmem_ld32(tmem + lane_off + C::COL_DQ + x * D + 32 * c, o);
+        if (u > 0) {
+          tmem_ld32(tmem + lane_off + C::COL_DQ + 32 * c, o);
           tmem_ld_wait();
         } else {
 #pragma unroll
@@ -817,7 +784,7 @@ static cudaError_t launch_bwd_t(const BwdLaunch& L, cudaStream_t st) {
   {
     auto kern = dq_kernel<D, BF16>;
     if ((e = set_smem(kern, DqCfg<D>::SMEM)) != cudaSuccess) return e;
-    kern<<<dim3((S + 2 * kTile - 1) / (2 * kTile), H, B), 320, DqCfg<D>::SMEM, st>>>(qp);
+    kern<<<dim3(qp.n_qtiles, H, B), 320, DqCfg<D>::SMEM, st>>>(qp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   return cudaSuccess;
