@@ -18,7 +18,8 @@
 //   keypass<LOCAL>   one CTA per 128-key tile: dK / dV over the local band,
 //                    then folds in dG of the tile's strided key and of every
 //                    relay row whose source lies in the tile, and stores.
-//   dq_kernel        one CTA per 128-query tile: dQ over band + global prefix.
+//   dq_kernel        persistent (one CTA per SM) over 128-query tiles: dQ over
+//                    band + global prefix.
 // The result is deterministic: every sum has a fixed order.
 //
 // The attention kernels use the warp roles of the forward (fwd.cu): warp 0
@@ -74,14 +75,20 @@ __global__ void __launch_bounds__(256) delta_kernel(const void* __restrict__ op,
 }
 
 // ===========================================================================
-// dQ: query-centric.  A CTA owns one 128-query tile and walks the forward's
-// key tiles (band, then global prefix) in 64-key units, skipping halves no row
-// needs.  Per unit: S = Q K_u^T and dP = dO V_u^T into one of two TMEM slots;
-// the softmax writes dS = P * (dP - Di) (P from the stored lse, 16-bit) back
-// into the slot; dQ += dS K_u reads dS from TMEM (TS-form MMA), so only K_u
-// comes from shared memory.  The two softmax warpgroups take alternate units
-// (the backward softmax has no running state).  A slot is reused once the dQ
-// product that read it has completed.
+// dQ: query-centric, persistent.  One CTA per SM walks query tiles t =
+// blockIdx.x, blockIdx.x + gridDim.x, ... (each a 128-query tile of one
+// (b, h), longest tiles first) and, per tile, the forward's key tiles (band,
+// then global prefix) in 64-key units, skipping halves no row needs.  Per
+// unit: S = Q K_u^T and dP = dO V_u^T into TMEM slot u & 1; softmax
+// warpgroup u & 1 writes dS = P * (dP - Di) (P from the stored lse, 16-bit)
+// back over S; dQ += dS K_u reads dS from TMEM (TS-form MMA) and accumulates
+// into one of two dQ accumulators (alternating tiles), which an epilogue
+// warpgroup drains to global memory while the next tile runs.  The K/V unit
+// stream, the S/dP -> softmax -> dQ pipeline and the epilogue all run across
+// tile boundaries, so no per-tile start-up or drain is exposed.
+//
+// Warps: 0 producer (TMA), 1 MMA issuer, 2-5 / 6-9 softmax (units of parity
+// 0 / 1), 10-13 epilogue.  TMEM lane = 32 * (warp % 4) + lane = query row.
 // ===========================================================================
 struct DqUnits {
   int m0, nband, ntiles, ls0, qmax, cmax;
@@ -106,38 +113,52 @@ struct DqUnits {
   }
 };
 
+// Query tile t of the persistent dQ walk: consecutive t are consecutive tiles
+// of one (b, h) (their band keys overlap in L2), latest queries first.
+struct DqTile {
+  int m0, h, b;
+  __device__ __forceinline__ DqTile(int t, int n_qtiles, int H) {
+    const int qt = n_qtiles - 1 - t % n_qtiles;
+    const int bh = t / n_qtiles;
+    m0 = qt * kTile;
+    h = bh % H;
+    b = bh / H;
+  }
+};
+
 template <int D>
 struct DqCfg {
   static constexpr int TB = kTile * D * 2;   // Q / dO tile
   static constexpr int UB = kUnit * D * 2;   // one K or V unit
   static constexpr int NSLOT = (D == 128) ? 10 : 20;  // ring entries K_0, V_0, K_1, V_1, ...
+  static constexpr int QPRE = 2;  // units of a new tile fetched before its Q / dO
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_DO = OFF_Q + TB;
   static constexpr int OFF_RING = OFF_DO + TB;
   static constexpr int OFF_BAR = OFF_RING + NSLOT * UB;
-  static constexpr int B_QFULL = 0, B_FULL = 1, B_EMPTY = 1 + NSLOT, B_SFULL = 1 + 2 * NSLOT, B_DSFULL = B_SFULL + 2,
-                       B_DQDONE = B_DSFULL + 2, B_DONE = B_DQDONE + 2, B_DRAIN = B_DONE + 1, N_BAR = B_DRAIN + 1;
+  static constexpr int B_QFULL = 0, B_QEMPTY = 1, B_FULL = 2, B_EMPTY = 2 + NSLOT, B_SFULL = 2 + 2 * NSLOT,
+                       B_DSFULL = B_SFULL + 2, B_DQDONE = B_DSFULL + 2, B_ACCFULL = B_DQDONE + 2,
+                       B_ACCFREE = B_ACCFULL + 2, B_DRAIN = B_ACCFREE + 2, N_BAR = B_DRAIN + 1;
   static constexpr int OFF_MISC = OFF_BAR + N_BAR * 8;
   static constexpr int SMEM = OFF_MISC + 16 + 1024;
   // TMEM: slot s -> S at 128 s, dP at 128 s + 64 (fp32, 64 columns each; dS
-  // overwrites the first 32 columns of S as 16-bit pairs); dQ at 256
+  // overwrites the first 32 columns of S as 16-bit pairs); dQ accumulator a
+  // at 256 + 128 a
   static constexpr int COL_DQ = 256;
+  static constexpr int THREADS = 448;
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
 template <int D, bool BF16>
-__global__ void __launch_bounds__(320, 1) dq_kernel(const __grid_constant__ QueryPassParams p) {
+__global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ QueryPassParams p) {
   using C = DqCfg<D>;
   using E = Elt<BF16>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = p.n_qtiles - 1 - static_cast<int>(blockIdx.x);  // longest tiles first
-  const int h = blockIdx.y, b = blockIdx.z, hk = h / p.kv_groups;
-  const int m0 = qt * kTile;
   const int W = p.W, S = p.S, R = p.R;
   const int Spad = p.n_qtiles * kTile;
-  const DqUnits un(m0, S, W, R);
+  const int n_tiles = p.n_qtiles * p.H * p.B;
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + C::OFF_BAR;
   auto BAR = [&](int i) { return bar0 + 8u * i; };
@@ -147,6 +168,7 @@ __global__ void __launch_bounds__(320, 1) dq_kernel(const __grid_constant__ Quer
 
   if (threadIdx.x == 0) {
     mbar_init(BAR(C::B_QFULL), 1);
+    mbar_init(BAR(C::B_QEMPTY), 1);
     for (int i = 0; i < C::NSLOT; ++i) {
       mbar_init(BAR(C::B_FULL + i), 1);
       mbar_init(BAR(C::B_EMPTY + i), 1);
@@ -155,8 +177,9 @@ __global__ void __launch_bounds__(320, 1) dq_kernel(const __grid_constant__ Quer
       mbar_init(BAR(C::B_SFULL + s), 1);
       mbar_init(BAR(C::B_DSFULL + s), 128);
       mbar_init(BAR(C::B_DQDONE + s), 1);
+      mbar_init(BAR(C::B_ACCFULL + s), 1);
+      mbar_init(BAR(C::B_ACCFREE + s), 128);
     }
-    mbar_init(BAR(C::B_DONE), 1);
     mbar_init(BAR(C::B_DRAIN), 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -168,174 +191,212 @@ __global__ void __launch_bounds__(320, 1) dq_kernel(const __grid_constant__ Quer
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
+    // ---------------- producer ----------------
     if (lane == 0) {
-      mbar_expect_tx(BAR(C::B_QFULL), 2 * C::TB);
-      for (int c = 0; c < D / 64; ++c) {
-        tma_load_4d(sbase + C::OFF_Q + c * kTile * 128, &p.tm_q, BAR(C::B_QFULL), c * 64, m0, h, b);
-        tma_load_4d(sbase + C::OFF_DO + c * kTile * 128, &p.tm_do, BAR(C::B_QFULL), c * 64, m0, h, b);
-      }
-      int e = 0;
+      int e = 0, nq = 0;  // ring entries issued, Q / dO tiles issued
       bool ok = true;
-      for (int j = 0; ok && j < un.ntiles; ++j)
-        for (int hh = 0; hh < 2 && ok; ++hh) {
-          int row0;
-          bool g;
-          if (!un.get(j, hh, row0, g)) continue;
-          for (int kv = 0; kv < 2; ++kv, ++e) {
-            const int sl = e % C::NSLOT;
-            if (e >= C::NSLOT && !mbar_wait(BAR(C::B_EMPTY + sl), ((e / C::NSLOT) - 1) & 1, ab)) { ok = false; break; }
-            const CUtensorMap* m = g ? (kv ? &p.tm_gv : &p.tm_gk) : (kv ? &p.tm_v : &p.tm_k);
-            mbar_expect_tx(BAR(C::B_FULL + sl), C::UB);
-            for (int c = 0; c < D / 64; ++c)
-              tma_load_4d(sbase + C::OFF_RING + sl * C::UB + c * kUnit * 128, m, BAR(C::B_FULL + sl), c * 64, row0,
-                          hk, b);
+      for (int t = blockIdx.x, it = 0; ok && t < n_tiles; t += gridDim.x, ++it) {
+        const DqTile tl(t, p.n_qtiles, p.H);
+        const int hk = tl.h / p.kv_groups;
+        const DqUnits un(tl.m0, S, W, R);
+        auto load_q = [&]() -> bool {
+          if (it > 0 && !mbar_wait(BAR(C::B_QEMPTY), (it - 1) & 1, ab)) return false;
+          mbar_expect_tx(BAR(C::B_QFULL), 2 * C::TB);
+          for (int c = 0; c < D / 64; ++c) {
+            tma_load_4d(sbase + C::OFF_Q + c * kTile * 128, &p.tm_q, BAR(C::B_QFULL), c * 64, tl.m0, tl.h, tl.b);
+            tma_load_4d(sbase + C::OFF_DO + c * kTile * 128, &p.tm_do, BAR(C::B_QFULL), c * 64, tl.m0, tl.h, tl.b);
           }
-        }
-      if (*abort_flag)
+          ++nq;
+          return true;
+        };
+        int lu = 0;  // units of this tile issued
+        for (int j = 0; ok && j < un.ntiles; ++j)
+          for (int hh = 0; hh < 2 && ok; ++hh) {
+            int row0;
+            bool g;
+            if (!un.get(j, hh, row0, g)) continue;
+            if (lu++ == C::QPRE && !load_q()) { ok = false; break; }
+            for (int kv = 0; kv < 2; ++kv, ++e) {
+              const int sl = e % C::NSLOT;
+              if (e >= C::NSLOT && !mbar_wait(BAR(C::B_EMPTY + sl), ((e / C::NSLOT) - 1) & 1, ab)) {
+                ok = false;
+                break;
+              }
+              const CUtensorMap* m = g ? (kv ? &p.tm_gv : &p.tm_gk) : (kv ? &p.tm_v : &p.tm_k);
+              mbar_expect_tx(BAR(C::B_FULL + sl), C::UB);
+              for (int c = 0; c < D / 64; ++c)
+                tma_load_4d(sbase + C::OFF_RING + sl * C::UB + c * kUnit * 128, m, BAR(C::B_FULL + sl), c * 64,
+                            row0, hk, tl.b);
+            }
+          }
+        if (ok && lu <= C::QPRE && !load_q()) ok = false;
+      }
+      if (*abort_flag) {  // let copies in flight land before the CTA exits
         for (int i = (e > C::NSLOT ? e - C::NSLOT : 0); i < e; ++i)
           mbar_wait_bounded(BAR(C::B_FULL + i % C::NSLOT), (i / C::NSLOT) & 1);
+        if (nq > 0) mbar_wait_bounded(BAR(C::B_QFULL), (nq - 1) & 1);
+      }
     }
     __syncwarp();
   } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t ID_S = idesc_f16(BF16, kTile, kUnit, false, false);
       constexpr uint32_t ID_Q = idesc_f16(BF16, kTile, D, false, true);
       const uint32_t qs = sbase + C::OFF_Q, dos = sbase + C::OFF_DO;
-      bool ok = mbar_wait(BAR(C::B_QFULL), 0, ab);
-      // dQ += dS K for unit i (its K sits in ring entry 2 i)
-      auto issue_dq = [&](int i) -> bool {
-        const int sl = i & 1, ek = (2 * i) % C::NSLOT;
+      bool ok = true;
+      // dQ += dS K for unit i of tile iteration iti (its K sits in ring entry 2 i)
+      auto issue_dq = [&](int i, int iti, bool first, bool last) -> bool {
+        const int sl = i & 1, ek = (2 * i) % C::NSLOT, acc = iti & 1;
         if (!mbar_wait(BAR(C::B_DSFULL + sl), (i >> 1) & 1, ab)) return false;
+        if (first && iti >= 2 && !mbar_wait(BAR(C::B_ACCFREE + acc), ((iti >> 1) - 1) & 1, ab)) return false;
         tc_fence_after();
         const uint32_t ks = sbase + C::OFF_RING + ek * C::UB;
 #pragma unroll
         for (int kk = 0; kk < kUnit / 16; ++kk)
-          mma_ts(tmem + C::COL_DQ, tmem + 128 * sl + kk * 8, sdesc(ks + kk * 16 * 128, kUnit * 128, 1024), ID_Q,
-                 (i > 0 || kk > 0) ? 1u : 0u);
+          mma_ts(tmem + C::COL_DQ + 128 * acc, tmem + 128 * sl + kk * 8, sdesc(ks + kk * 16 * 128, kUnit * 128, 1024),
+                 ID_Q, (!first || kk > 0) ? 1u : 0u);
         mma_commit(BAR(C::B_DQDONE + sl));
         mma_commit(BAR(C::B_EMPTY + ek));
+        if (last) mma_commit(BAR(C::B_ACCFULL + acc));
         return true;
       };
-      int u = 0;
-      for (int j = 0; ok && j < un.ntiles; ++j)
-        for (int hh = 0; ok && hh < 2; ++hh) {
-          int row0;
-          bool g;
-          if (!un.get(j, hh, row0, g)) continue;
-          const int sl = u & 1, ek = 2 * u, ev = 2 * u + 1;
-          if (!mbar_wait(BAR(C::B_FULL + ek % C::NSLOT), (ek / C::NSLOT) & 1, ab) ||
-              !mbar_wait(BAR(C::B_FULL + ev % C::NSLOT), (ev / C::NSLOT) & 1, ab) ||
-              (u >= 2 && !mbar_wait(BAR(C::B_DQDONE + sl), ((u >> 1) - 1) & 1, ab))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t ks = sbase + C::OFF_RING + (ek % C::NSLOT) * C::UB;
-          const uint32_t vs = sbase + C::OFF_RING + (ev % C::NSLOT) * C::UB;
+      int u = 0;                                     // units issued (all tiles)
+      int pit = -1;                                  // tile iteration of unit u - 1
+      bool pfirst = false;                           // unit u - 1 was its tile's first
+      for (int t = blockIdx.x, it = 0; ok && t < n_tiles; t += gridDim.x, ++it) {
+        const DqTile tl(t, p.n_qtiles, p.H);
+        const DqUnits un(tl.m0, S, W, R);
+        if (!mbar_wait(BAR(C::B_QFULL), it & 1, ab)) { ok = false; break; }
+        bool first = true;
+        for (int j = 0; ok && j < un.ntiles; ++j)
+          for (int hh = 0; ok && hh < 2; ++hh) {
+            int row0;
+            bool g;
+            if (!un.get(j, hh, row0, g)) continue;
+            const int sl = u & 1, ek = 2 * u, ev = 2 * u + 1;
+            if (!mbar_wait(BAR(C::B_FULL + ek % C::NSLOT), (ek / C::NSLOT) & 1, ab) ||
+                !mbar_wait(BAR(C::B_FULL + ev % C::NSLOT), (ev / C::NSLOT) & 1, ab) ||
+                (u >= 2 && !mbar_wait(BAR(C::B_DQDONE + sl), ((u >> 1) - 1) & 1, ab))) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t ks = sbase + C::OFF_RING + (ek % C::NSLOT) * C::UB;
+            const uint32_t vs = sbase + C::OFF_RING + (ev % C::NSLOT) * C::UB;
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t qo = (kk >> 2) * kTile * 128 + (kk & 3) * 32;
-            const uint32_t ko = (kk >> 2) * kUnit * 128 + (kk & 3) * 32;
-            mma_ss(tmem + 128 * sl, sdesc(qs + qo, 16, 1024), sdesc(ks + ko, 16, 1024), ID_S, kk > 0 ? 1u : 0u);
-            mma_ss(tmem + 128 * sl + 64, sdesc(dos + qo, 16, 1024), sdesc(vs + ko, 16, 1024), ID_S,
-                   kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t qo = (kk >> 2) * kTile * 128 + (kk & 3) * 32;
+              const uint32_t ko = (kk >> 2) * kUnit * 128 + (kk & 3) * 32;
+              mma_ss(tmem + 128 * sl, sdesc(qs + qo, 16, 1024), sdesc(ks + ko, 16, 1024), ID_S, kk > 0 ? 1u : 0u);
+              mma_ss(tmem + 128 * sl + 64, sdesc(dos + qo, 16, 1024), sdesc(vs + ko, 16, 1024), ID_S,
+                     kk > 0 ? 1u : 0u);
+            }
+            mma_commit(BAR(C::B_SFULL + sl));
+            mma_commit(BAR(C::B_EMPTY + ev % C::NSLOT));  // V_u is no longer needed
+            // dQ of the previous unit (possibly the previous tile's last)
+            if (u > 0 && !issue_dq(u - 1, pit, pfirst, pit != it)) { ok = false; break; }
+            pit = it;
+            pfirst = first;
+            first = false;
+            ++u;
           }
-          mma_commit(BAR(C::B_SFULL + sl));
-          mma_commit(BAR(C::B_EMPTY + ev % C::NSLOT));  // V_u is no longer needed
-          if (u > 0 && !issue_dq(u - 1)) { ok = false; break; }
-          ++u;
-        }
-      if (ok && u > 0) ok = issue_dq(u - 1);
-      if (ok) mma_commit(BAR(C::B_DONE));
+        if (ok) mma_commit(BAR(C::B_QEMPTY));  // every S / dP of this tile issued
+      }
+      if (ok && u > 0) ok = issue_dq(u - 1, pit, pfirst, true);
       if (!ok) {
         mma_commit(BAR(C::B_DRAIN));
         mbar_wait_bounded(BAR(C::B_DRAIN), 0);
       }
     }
     __syncwarp();
-  } else {
-    const int w = (warp - 2) >> 2;           // softmax warpgroup: units with (u & 1) == w
-    const int r = ((warp & 3) << 5) | lane;  // query row = TMEM lane
-    const int qi = m0 + r;
-    const bool row_ok = qi < S;
-    const int ls = local_start(qi, W);
-    const int cnt = gcount(qi, W, R);
-    const uint32_t lane_off = static_cast<uint32_t>(r & ~31) << 16;
-    const uint32_t scol = tmem + lane_off + 128 * w;
+  } else if (warp < 10) {
+    // ---------------- softmax: dS = P * (dP - Di) ----------------
+    const int w = (warp - 2) >> 2;           // units with (u & 1) == w, TMEM slot w
+    const int r = ((warp & 3) << 5) | lane;  // query row within the tile = TMEM lane
+    const uint32_t scol = tmem + (static_cast<uint32_t>(r & ~31) << 16) + 128 * w;
     const float sl2 = p.scale_log2;
-    const int64_t rowi = (static_cast<int64_t>(b) * p.H + h) * Spad + qi;
-    const float lse2 = p.lse[rowi];  // lse * log2(e), padded array
-    const float di = p.delta[rowi];
     bool ok = true;
     int u = 0;
-    for (int j = 0; ok && j < un.ntiles; ++j)
-      for (int hh = 0; hh < 2; ++hh) {
-        int row0;
-        bool g;
-        if (!un.get(j, hh, row0, g)) continue;
-        const int uu = u++;
-        if ((uu & 1) != w) continue;
-        if (!mbar_wait(BAR(C::B_SFULL + w), (uu >> 1) & 1, ab)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        int lo, hi;
-        if (!g) {
-          lo = ls - row0;
-          hi = qi - row0 + 1;
-        } else {
-          lo = 0;
-          hi = cnt - row0;
-        }
-        if (!row_ok) { lo = 0; hi = 0; }
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          float s[32], dp[32];
-          tmem_ld32(scol + 32 * c, s);
-          tmem_ld32(scol + 64 + 32 * c, dp);
-          tmem_ld_wait();
-          uint32_t pk[16];
-#pragma unroll
-          for (int e2 = 0; e2 < 32; e2 += 2) {
-            const int col = 32 * c + e2;
-            const float p0 = (col >= lo && col < hi) ? ex2(fmaf(s[e2], sl2, -lse2)) : 0.f;
-            const float p1 = (col + 1 >= lo && col + 1 < hi) ? ex2(fmaf(s[e2 + 1], sl2, -lse2)) : 0.f;
-            pk[e2 / 2] = E::pack(p0 * (dp[e2] - di), p1 * (dp[e2 + 1] - di));
+    for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x) {
+      const DqTile tl(t, p.n_qtiles, p.H);
+      const DqUnits un(tl.m0, S, W, R);
+      const int qi = tl.m0 + r;
+      const bool row_ok = qi < S;
+      const int ls = local_start(qi, W);
+      const int cnt = gcount(qi, W, R);
+      const int64_t rowi = (static_cast<int64_t>(tl.b) * p.H + tl.h) * Spad + qi;
+      const float lse2 = p.lse[rowi];  // lse * log2(e), padded array
+      const float di = p.delta[rowi];
+      for (int j = 0; ok && j < un.ntiles; ++j)
+        for (int hh = 0; hh < 2; ++hh) {
+          int row0;
+          bool g;
+          if (!un.get(j, hh, row0, g)) continue;
+          const int uu = u++;
+          if ((uu & 1) != w) continue;
+          if (!mbar_wait(BAR(C::B_SFULL + w), (uu >> 1) & 1, ab)) {
+            ok = false;
+            break;
           }
-          // chunk c of dS overwrites S columns [16c, 16c+16), already read
-          tmem_st16(scol + 16 * c, pk);
+          tc_fence_after();
+          int lo, hi;
+          if (!g) {
+            lo = ls - row0;
+            hi = qi - row0 + 1;
+          } else {
+            lo = 0;
+            hi = cnt - row0;
+          }
+          if (!row_ok) { lo = 0; hi = 0; }
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            float s[32], dp[32];
+            tmem_ld32(scol + 32 * c, s);
+            tmem_ld32(scol + 64 + 32 * c, dp);
+            tmem_ld_wait();
+            uint32_t pk[16];
+#pragma unroll
+            for (int e2 = 0; e2 < 32; e2 += 2) {
+              const int col = 32 * c + e2;
+              const float p0 = (col >= lo && col < hi) ? ex2(fmaf(s[e2], sl2, -lse2)) : 0.f;
+              const float p1 = (col + 1 >= lo && col + 1 < hi) ? ex2(fmaf(s[e2 + 1], sl2, -lse2)) : 0.f;
+              pk[e2 / 2] = E::pack(p0 * (dp[e2] - di), p1 * (dp[e2 + 1] - di));
+            }
+            tmem_st16(scol + 16 * c, pk);  // dS over S columns [16c, 16c+16), already read
+          }
+          tmem_st_wait();
+          tc_fence_before();
+          mbar_arrive(BAR(C::B_DSFULL + w));
         }
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(BAR(C::B_DSFULL + w));
-      }
-    // epilogue: warpgroup w writes columns [w * D/2, (w+1) * D/2) of dQ
-    if (ok && (u == 0 || mbar_wait(BAR(C::B_DONE), 0, ab))) {
+    }
+  } else {
+    // ---------------- epilogue: dQ accumulator -> global ----------------
+    const int r = ((warp & 3) << 5) | lane;
+    const uint32_t lane_off = static_cast<uint32_t>(r & ~31) << 16;
+    for (int t = blockIdx.x, it = 0; t < n_tiles; t += gridDim.x, ++it) {
+      const DqTile tl(t, p.n_qtiles, p.H);
+      const int acc = it & 1;
+      if (!mbar_wait(BAR(C::B_ACCFULL + acc), (it >> 1) & 1, ab)) break;
       tc_fence_after();
-      typename E::T* orow = reinterpret_cast<typename E::T*>(p.out) + b * p.out_sb + h * p.out_sh +
-                            static_cast<int64_t>(qi) * p.out_ss;
-#pragma unroll 1
-      for (int c = w * (D / 64); c < (w + 1) * (D / 64); ++c) {
+      uint32_t pk[D / 2];
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
         float o[32];
-        if (u > 0) {
-          tmem_ld32(tmem + lane_off + C::COL_DQ + 32 * c, o);
-          tmem_ld_wait();
-        } else {
+        tmem_ld32(tmem + lane_off + C::COL_DQ + 128 * acc + 32 * c, o);
+        tmem_ld_wait();
 #pragma unroll
-          for (int e2 = 0; e2 < 32; ++e2) o[e2] = 0.f;
-        }
-        if (row_ok) {
+        for (int e2 = 0; e2 < 32; e2 += 2) pk[16 * c + e2 / 2] = E::pack(o[e2] * p.scale, o[e2 + 1] * p.scale);
+      }
+      tc_fence_before();
+      mbar_arrive(BAR(C::B_ACCFREE + acc));
+      const int qi = tl.m0 + r;
+      if (qi < S) {
+        typename E::T* orow = reinterpret_cast<typename E::T*>(p.out) + tl.b * p.out_sb + tl.h * p.out_sh +
+                              static_cast<int64_t>(qi) * p.out_ss;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 v4;
-            v4.x = E::pack(o[8 * q + 0] * p.scale, o[8 * q + 1] * p.scale);
-            v4.y = E::pack(o[8 * q + 2] * p.scale, o[8 * q + 3] * p.scale);
-            v4.z = E::pack(o[8 * q + 4] * p.scale, o[8 * q + 5] * p.scale);
-            v4.w = E::pack(o[8 * q + 6] * p.scale, o[8 * q + 7] * p.scale);
-            *reinterpret_cast<uint4*>(orow + 32 * c + 8 * q) = v4;
-          }
-        }
+        for (int q = 0; q < D / 8; ++q)
+          *reinterpret_cast<uint4*>(orow + 8 * q) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
       }
     }
   }
@@ -735,6 +796,20 @@ __global__ void __launch_bounds__(256) dalpha_kernel(const float* __restrict__ d
 // ===========================================================================
 // host side
 // ===========================================================================
+// SMs of the current device (cached per device).
+static int sm_count() {
+  static int cache[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (cache[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
 template <typename K>
 static cudaError_t set_smem(K kern, int bytes) {
   return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
@@ -784,7 +859,8 @@ static cudaError_t launch_bwd_t(const BwdLaunch& L, cudaStream_t st) {
   {
     auto kern = dq_kernel<D, BF16>;
     if ((e = set_smem(kern, DqCfg<D>::SMEM)) != cudaSuccess) return e;
-    kern<<<dim3(qp.n_qtiles, H, B), 320, DqCfg<D>::SMEM, st>>>(qp);
+    const int n_tiles = qp.n_qtiles * H * B;
+    kern<<<dim3(n_tiles < sm_count() ? n_tiles : sm_count()), DqCfg<D>::THREADS, DqCfg<D>::SMEM, st>>>(qp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   return cudaSuccess;
