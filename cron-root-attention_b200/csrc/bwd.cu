@@ -90,6 +90,21 @@ __global__ void __launch_bounds__(256) delta_kernel(const void* __restrict__ op,
 // Warps: 0 producer (TMA), 1 MMA issuer, 2-5 / 6-9 softmax (units of parity
 // 0 / 1), 10-13 epilogue.  TMEM lane = 32 * (warp % 4) + lane = query row.
 // ===========================================================================
+// Optional cycle counters of the dQ pass (build with -DCRA_PROF; read with
+// cra_dq_prof): per role, cycles spent waiting on each barrier and working.
+#ifdef CRA_PROF
+__device__ unsigned long long g_dq_prof[32];
+#define PROF_T(v) const unsigned long long v = clock64()
+#define PROF_ADD(k, t0) \
+  if ((threadIdx.x & 31) == 0) atomicAdd(&g_dq_prof[k], clock64() - (t0))
+#define PROF_CNT(k, n) \
+  if ((threadIdx.x & 31) == 0) atomicAdd(&g_dq_prof[k], static_cast<unsigned long long>(n))
+#else
+#define PROF_T(v)
+#define PROF_ADD(k, t0)
+#define PROF_CNT(k, n)
+#endif
+
 struct DqUnits {
   int m0, nband, ntiles, ls0, qmax, cmax;
   __device__ __forceinline__ DqUnits(int m0_, int S, int W, int R) : m0(m0_) {
@@ -137,7 +152,7 @@ struct DqCfg {
   static constexpr int OFF_RING = OFF_DO + TB;
   static constexpr int OFF_BAR = OFF_RING + NSLOT * UB;
   static constexpr int B_QFULL = 0, B_QEMPTY = 1, B_FULL = 2, B_EMPTY = 2 + NSLOT, B_SFULL = 2 + 2 * NSLOT,
-                       B_DSFULL = B_SFULL + 2, B_DQDONE = B_DSFULL + 2, B_ACCFULL = B_DQDONE + 2,
+                       B_DSFULL = B_SFULL + 2, B_ACCFULL = B_DSFULL + 2,
                        B_ACCFREE = B_ACCFULL + 2, B_DRAIN = B_ACCFREE + 2, N_BAR = B_DRAIN + 1;
   static constexpr int OFF_MISC = OFF_BAR + N_BAR * 8;
   static constexpr int SMEM = OFF_MISC + 16 + 1024;
@@ -176,7 +191,6 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
     for (int s = 0; s < 2; ++s) {
       mbar_init(BAR(C::B_SFULL + s), 1);
       mbar_init(BAR(C::B_DSFULL + s), 128);
-      mbar_init(BAR(C::B_DQDONE + s), 1);
       mbar_init(BAR(C::B_ACCFULL + s), 1);
       mbar_init(BAR(C::B_ACCFREE + s), 128);
     }
@@ -200,7 +214,9 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
         const int hk = tl.h / p.kv_groups;
         const DqUnits un(tl.m0, S, W, R);
         auto load_q = [&]() -> bool {
+          PROF_T(t0);
           if (it > 0 && !mbar_wait(BAR(C::B_QEMPTY), (it - 1) & 1, ab)) return false;
+          PROF_ADD(0, t0);
           mbar_expect_tx(BAR(C::B_QFULL), 2 * C::TB);
           for (int c = 0; c < D / 64; ++c) {
             tma_load_4d(sbase + C::OFF_Q + c * kTile * 128, &p.tm_q, BAR(C::B_QFULL), c * 64, tl.m0, tl.h, tl.b);
@@ -218,10 +234,12 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
             if (lu++ == C::QPRE && !load_q()) { ok = false; break; }
             for (int kv = 0; kv < 2; ++kv, ++e) {
               const int sl = e % C::NSLOT;
+              PROF_T(t0);
               if (e >= C::NSLOT && !mbar_wait(BAR(C::B_EMPTY + sl), ((e / C::NSLOT) - 1) & 1, ab)) {
                 ok = false;
                 break;
               }
+              PROF_ADD(1, t0);
               const CUtensorMap* m = g ? (kv ? &p.tm_gv : &p.tm_gk) : (kv ? &p.tm_v : &p.tm_k);
               mbar_expect_tx(BAR(C::B_FULL + sl), C::UB);
               for (int c = 0; c < D / 64; ++c)
@@ -240,34 +258,43 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
     __syncwarp();
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    {  // whole warp, converged; one elected lane issues
       constexpr uint32_t ID_S = idesc_f16(BF16, kTile, kUnit, false, false);
       constexpr uint32_t ID_Q = idesc_f16(BF16, kTile, D, false, true);
-      const uint32_t qs = sbase + C::OFF_Q, dos = sbase + C::OFF_DO;
+      // shared-memory descriptors: the start-address field (bits 0-13, in 16-byte
+      // units) of a base descriptor plus a constant offset never carries, as
+      // shared memory ends below 256 KB
+      const uint64_t qd = sdesc(sbase + C::OFF_Q, 16, 1024), dd = sdesc(sbase + C::OFF_DO, 16, 1024);
       bool ok = true;
       // dQ += dS K for unit i of tile iteration iti (its K sits in ring entry 2 i)
       auto issue_dq = [&](int i, int iti, bool first, bool last) -> bool {
         const int sl = i & 1, ek = (2 * i) % C::NSLOT, acc = iti & 1;
-        if (!mbar_wait(BAR(C::B_DSFULL + sl), (i >> 1) & 1, ab)) return false;
-        if (first && iti >= 2 && !mbar_wait(BAR(C::B_ACCFREE + acc), ((iti >> 1) - 1) & 1, ab)) return false;
+        PROF_T(t0);
+        if (!warp_wait(BAR(C::B_DSFULL + sl), (i >> 1) & 1, ab)) return false;
+        PROF_ADD(4, t0);
+        PROF_T(t1);
+        if (first && iti >= 2 && !warp_wait(BAR(C::B_ACCFREE + acc), ((iti >> 1) - 1) & 1, ab)) return false;
+        PROF_ADD(5, t1);
         tc_fence_after();
-        const uint32_t ks = sbase + C::OFF_RING + ek * C::UB;
+        const uint64_t kd = sdesc(sbase + C::OFF_RING + ek * C::UB, kUnit * 128, 1024);
 #pragma unroll
         for (int kk = 0; kk < kUnit / 16; ++kk)
-          mma_ts(tmem + C::COL_DQ + 128 * acc, tmem + 128 * sl + kk * 8, sdesc(ks + kk * 16 * 128, kUnit * 128, 1024),
-                 ID_Q, (!first || kk > 0) ? 1u : 0u);
-        mma_commit(BAR(C::B_DQDONE + sl));
-        mma_commit(BAR(C::B_EMPTY + ek));
-        if (last) mma_commit(BAR(C::B_ACCFULL + acc));
+          mma_ts_w(tmem + C::COL_DQ + 128 * acc, tmem + 128 * sl + kk * 8, kd + ((kk * 16 * 128) >> 4), ID_Q,
+                 (!first || kk > 0) ? 1u : 0u);
+        mma_commit_w(BAR(C::B_EMPTY + ek));
+        if (last) mma_commit_w(BAR(C::B_ACCFULL + acc));
         return true;
       };
+      PROF_T(tstart);
       int u = 0;                                     // units issued (all tiles)
       int pit = -1;                                  // tile iteration of unit u - 1
       bool pfirst = false;                           // unit u - 1 was its tile's first
       for (int t = blockIdx.x, it = 0; ok && t < n_tiles; t += gridDim.x, ++it) {
         const DqTile tl(t, p.n_qtiles, p.H);
         const DqUnits un(tl.m0, S, W, R);
-        if (!mbar_wait(BAR(C::B_QFULL), it & 1, ab)) { ok = false; break; }
+        PROF_T(tq);
+        if (!warp_wait(BAR(C::B_QFULL), it & 1, ab)) { ok = false; break; }
+        PROF_ADD(6, tq);
         bool first = true;
         for (int j = 0; ok && j < un.ntiles; ++j)
           for (int hh = 0; ok && hh < 2; ++hh) {
@@ -275,25 +302,32 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
             bool g;
             if (!un.get(j, hh, row0, g)) continue;
             const int sl = u & 1, ek = 2 * u, ev = 2 * u + 1;
-            if (!mbar_wait(BAR(C::B_FULL + ek % C::NSLOT), (ek / C::NSLOT) & 1, ab) ||
-                !mbar_wait(BAR(C::B_FULL + ev % C::NSLOT), (ev / C::NSLOT) & 1, ab) ||
-                (u >= 2 && !mbar_wait(BAR(C::B_DQDONE + sl), ((u >> 1) - 1) & 1, ab))) {
+            // Slot sl was last read by dQ(u - 2), issued before this S / dP:
+            // MMAs issued by this warp execute in issue order, so no wait is needed
+            // (a wait on a commit would also wait for S / dP(u - 1), issued
+            // before dQ(u - 2), and drain the tensor pipe every unit).
+            PROF_T(t0);
+            if (!warp_wait(BAR(C::B_FULL + ek % C::NSLOT), (ek / C::NSLOT) & 1, ab) ||
+                !warp_wait(BAR(C::B_FULL + ev % C::NSLOT), (ev / C::NSLOT) & 1, ab)) {
               ok = false;
               break;
             }
+            PROF_ADD(7, t0);
+            PROF_T(t1);
             tc_fence_after();
-            const uint32_t ks = sbase + C::OFF_RING + (ek % C::NSLOT) * C::UB;
-            const uint32_t vs = sbase + C::OFF_RING + (ev % C::NSLOT) * C::UB;
+            const uint64_t kd = sdesc(sbase + C::OFF_RING + (ek % C::NSLOT) * C::UB, 16, 1024);
+            const uint64_t vd = sdesc(sbase + C::OFF_RING + (ev % C::NSLOT) * C::UB, 16, 1024);
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
-              const uint32_t qo = (kk >> 2) * kTile * 128 + (kk & 3) * 32;
-              const uint32_t ko = (kk >> 2) * kUnit * 128 + (kk & 3) * 32;
-              mma_ss(tmem + 128 * sl, sdesc(qs + qo, 16, 1024), sdesc(ks + ko, 16, 1024), ID_S, kk > 0 ? 1u : 0u);
-              mma_ss(tmem + 128 * sl + 64, sdesc(dos + qo, 16, 1024), sdesc(vs + ko, 16, 1024), ID_S,
-                     kk > 0 ? 1u : 0u);
+              // K-step kk: 64-column chunk kk / 4, 32-byte step kk % 4 in its 128-byte rows
+              const uint32_t qo = ((kk >> 2) * kTile * 128 + (kk & 3) * 32) >> 4;
+              const uint32_t ko = ((kk >> 2) * kUnit * 128 + (kk & 3) * 32) >> 4;
+              mma_ss_w(tmem + 128 * sl, qd + qo, kd + ko, ID_S, kk > 0 ? 1u : 0u);
+              mma_ss_w(tmem + 128 * sl + 64, dd + qo, vd + ko, ID_S, kk > 0 ? 1u : 0u);
             }
-            mma_commit(BAR(C::B_SFULL + sl));
-            mma_commit(BAR(C::B_EMPTY + ev % C::NSLOT));  // V_u is no longer needed
+            mma_commit_w(BAR(C::B_SFULL + sl));
+            mma_commit_w(BAR(C::B_EMPTY + ev % C::NSLOT));  // V_u is no longer needed
+            PROF_ADD(8, t1);
             // dQ of the previous unit (possibly the previous tile's last)
             if (u > 0 && !issue_dq(u - 1, pit, pfirst, pit != it)) { ok = false; break; }
             pit = it;
@@ -301,11 +335,14 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
             first = false;
             ++u;
           }
-        if (ok) mma_commit(BAR(C::B_QEMPTY));  // every S / dP of this tile issued
+        if (ok) mma_commit_w(BAR(C::B_QEMPTY));  // every S / dP of this tile issued
       }
       if (ok && u > 0) ok = issue_dq(u - 1, pit, pfirst, true);
+      PROF_ADD(9, tstart);
+      PROF_CNT(30, u);
+      PROF_CNT(31, 1);
       if (!ok) {
-        mma_commit(BAR(C::B_DRAIN));
+        mma_commit_w(BAR(C::B_DRAIN));
         mbar_wait_bounded(BAR(C::B_DRAIN), 0);
       }
     }
@@ -335,10 +372,15 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
           if (!un.get(j, hh, row0, g)) continue;
           const int uu = u++;
           if ((uu & 1) != w) continue;
+          PROF_T(t0);
           if (!mbar_wait(BAR(C::B_SFULL + w), (uu >> 1) & 1, ab)) {
             ok = false;
             break;
           }
+#ifdef CRA_PROF
+          if (lane == 0) PROF_ADD(12, t0);
+#endif
+          PROF_T(t1);
           tc_fence_after();
           int lo, hi;
           if (!g) {
@@ -368,6 +410,9 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
           tmem_st_wait();
           tc_fence_before();
           mbar_arrive(BAR(C::B_DSFULL + w));
+#ifdef CRA_PROF
+          if (lane == 0) PROF_ADD(13, t1);
+#endif
         }
     }
   } else {
@@ -377,7 +422,11 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
     for (int t = blockIdx.x, it = 0; t < n_tiles; t += gridDim.x, ++it) {
       const DqTile tl(t, p.n_qtiles, p.H);
       const int acc = it & 1;
+      PROF_T(t0);
       if (!mbar_wait(BAR(C::B_ACCFULL + acc), (it >> 1) & 1, ab)) break;
+#ifdef CRA_PROF
+      if (lane == 0) PROF_ADD(16, t0);
+#endif
       tc_fence_after();
       uint32_t pk[D / 2];
 #pragma unroll
@@ -405,6 +454,17 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
+
+#ifdef CRA_PROF
+extern "C" __attribute__((visibility("default"))) int cra_dq_prof(unsigned long long* out32, int reset) {
+  cudaMemcpyFromSymbol(out32, g_dq_prof, sizeof(g_dq_prof));
+  if (reset) {
+    unsigned long long z[32] = {};
+    cudaMemcpyToSymbol(g_dq_prof, z, sizeof(z));
+  }
+  return 0;
+}
+#endif
 
 // ===========================================================================
 // Key-centric pass.  Thread r owns key row r of the CTA's 128-row key tile
