@@ -474,8 +474,10 @@ extern "C" __attribute__((visibility("default"))) int cra_dq_prof(unsigned long 
 //   P^T, dS^T (16-bit) written back into the same TMEM slot,
 //   dV += P^T dO_u,  dK += dS^T Q_u  (TMEM accumulators; A operands read
 //   from TMEM, so only dO_u / Q_u come from shared memory).
-// The two softmax warpgroups take alternate units.  A slot is reused only
-// after the dV / dK products that read it have completed (GDONE).
+// The two softmax warpgroups take alternate units.  A slot is rewritten by
+// S^T / dP^T of unit u + 2 only after the dV / dK products of unit u that
+// read it were issued; MMAs issued by one warp execute in issue order, so no
+// completion wait is needed (one would drain the tensor pipe every unit).
 // ===========================================================================
 template <int D>
 struct KeyCfg {
@@ -488,7 +490,7 @@ struct KeyCfg {
   static constexpr int OFF_LSE = OFF_Q + NSQ * 2 * UB;  // stage s: lse2[64], delta[64]
   static constexpr int OFF_BAR = OFF_LSE + NSQ * 2 * kUnit * 4;
   static constexpr int B_KVFULL = 0, B_QFULL = 1, B_QEMPTY = 1 + NSQ, B_SFULL = 1 + 2 * NSQ, B_PFULL = B_SFULL + 2,
-                       B_GDONE = B_PFULL + 2, B_DONE = B_GDONE + 2, B_DRAIN = B_DONE + 1, N_BAR = B_DRAIN + 1;
+                       B_DONE = B_PFULL + 2, B_DRAIN = B_DONE + 1, N_BAR = B_DRAIN + 1;
   static constexpr int OFF_MISC = OFF_BAR + N_BAR * 8;
   static constexpr int SMEM = OFF_MISC + 16 + 1024;
   // TMEM: slot s -> S^T at 128 s, dP^T at 128 s + 64 (fp32, 64 columns each);
@@ -548,7 +550,6 @@ __global__ void __launch_bounds__(320, 1) keypass_kernel(const __grid_constant__
     for (int s = 0; s < 2; ++s) {
       mbar_init(BAR(C::B_SFULL + s), 1);
       mbar_init(BAR(C::B_PFULL + s), 128);
-      mbar_init(BAR(C::B_GDONE + s), 1);
     }
     mbar_init(BAR(C::B_DONE), 1);
     mbar_init(BAR(C::B_DRAIN), 1);
@@ -597,33 +598,32 @@ __global__ void __launch_bounds__(320, 1) keypass_kernel(const __grid_constant__
     }
     __syncwarp();
   } else if (warp == 1) {
-    if (lane == 0 && nU > 0) {
+    if (nU > 0) {  // whole warp, converged; one elected lane issues
       constexpr uint32_t ID_S = idesc_f16(BF16, kTile, kUnit, false, false);
       constexpr uint32_t ID_G = idesc_f16(BF16, kTile, D, false, true);
       const uint32_t ks = sbase + C::OFF_K, vs = sbase + C::OFF_V;
-      bool ok = mbar_wait(BAR(C::B_KVFULL), 0, ab);
+      bool ok = warp_wait(BAR(C::B_KVFULL), 0, ab);
       auto issue_kv = [&](int i) -> bool {
         const int st = i % C::NSQ, sl = i & 1;
-        if (!mbar_wait(BAR(C::B_PFULL + sl), (i >> 1) & 1, ab)) return false;
+        if (!warp_wait(BAR(C::B_PFULL + sl), (i >> 1) & 1, ab)) return false;
         tc_fence_after();
         const uint32_t qd = sbase + C::OFF_Q + st * 2 * C::UB;
 #pragma unroll
         for (int kk = 0; kk < kUnit / 16; ++kk) {
           const uint32_t boff = kk * 16 * 128;
-          mma_ts(tmem + C::COL_DV, tmem + 128 * sl + kk * 8, sdesc(qd + C::UB + boff, kUnit * 128, 1024), ID_G,
+          mma_ts_w(tmem + C::COL_DV, tmem + 128 * sl + kk * 8, sdesc(qd + C::UB + boff, kUnit * 128, 1024), ID_G,
                  (i > 0 || kk > 0) ? 1u : 0u);
-          mma_ts(tmem + C::COL_DK, tmem + 128 * sl + 64 + kk * 8, sdesc(qd + boff, kUnit * 128, 1024), ID_G,
+          mma_ts_w(tmem + C::COL_DK, tmem + 128 * sl + 64 + kk * 8, sdesc(qd + boff, kUnit * 128, 1024), ID_G,
                  (i > 0 || kk > 0) ? 1u : 0u);
         }
-        mma_commit(BAR(C::B_GDONE + sl));
-        mma_commit(BAR(C::B_QEMPTY + st));
+        mma_commit_w(BAR(C::B_QEMPTY + st));
         return true;
       };
       for (int u = 0; ok && u < nU; ++u) {
         const int st = u % C::NSQ, sl = u & 1;
-        // slot sl was last read by the dV / dK products of unit u - 2
-        if (!mbar_wait(BAR(C::B_QFULL + st), (u / C::NSQ) & 1, ab) ||
-            (u >= 2 && !mbar_wait(BAR(C::B_GDONE + sl), ((u >> 1) - 1) & 1, ab))) {
+        // slot sl was last read by the dV / dK products of unit u - 2, issued
+        // before this S^T / dP^T (in-order execution)
+        if (!warp_wait(BAR(C::B_QFULL + st), (u / C::NSQ) & 1, ab)) {
           ok = false;
           break;
         }
@@ -633,17 +633,17 @@ __global__ void __launch_bounds__(320, 1) keypass_kernel(const __grid_constant__
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t ko = (kk >> 2) * kTile * 128 + (kk & 3) * 32;
           const uint32_t qo = (kk >> 2) * kUnit * 128 + (kk & 3) * 32;
-          mma_ss(tmem + 128 * sl, sdesc(ks + ko, 16, 1024), sdesc(qd + qo, 16, 1024), ID_S, kk > 0 ? 1u : 0u);
-          mma_ss(tmem + 128 * sl + 64, sdesc(vs + ko, 16, 1024), sdesc(qd + C::UB + qo, 16, 1024), ID_S,
+          mma_ss_w(tmem + 128 * sl, sdesc(ks + ko, 16, 1024), sdesc(qd + qo, 16, 1024), ID_S, kk > 0 ? 1u : 0u);
+          mma_ss_w(tmem + 128 * sl + 64, sdesc(vs + ko, 16, 1024), sdesc(qd + C::UB + qo, 16, 1024), ID_S,
                  kk > 0 ? 1u : 0u);
         }
-        mma_commit(BAR(C::B_SFULL + sl));
+        mma_commit_w(BAR(C::B_SFULL + sl));
         if (u > 0 && !issue_kv(u - 1)) { ok = false; break; }
       }
       if (ok) ok = issue_kv(nU - 1);
-      if (ok) mma_commit(BAR(C::B_DONE));
+      if (ok) mma_commit_w(BAR(C::B_DONE));
       if (!ok) {
-        mma_commit(BAR(C::B_DRAIN));
+        mma_commit_w(BAR(C::B_DRAIN));
         mbar_wait_bounded(BAR(C::B_DRAIN), 0);
       }
     }

@@ -141,10 +141,10 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    {  // whole warp, converged; one elected lane issues
       constexpr uint32_t ID_S = idesc_f16(BF16, kTile, kTile, false, false);
       constexpr uint32_t ID_O = idesc_f16(BF16, kTile, D, false, true);
-      bool ok = mbar_wait(BAR(C::B_QFULL), 0, ab);
+      bool ok = warp_wait(BAR(C::B_QFULL), 0, ab);
       int ns[2] = {0, 0};   // score tiles issued per query tile
       int npv[2] = {0, 0};  // PV products issued per query tile
       auto issue_pv = [&](int j) -> bool {
@@ -152,23 +152,23 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
         bool g, use[2];
         sch.tile(j, row0, g, use[0], use[1]);
         const int i = 2 * j + 1, sl = i % C::NSLOT;
-        if (!mbar_wait(BAR(C::B_FULL + sl), (i / C::NSLOT) & 1, ab)) return false;
+        if (!warp_wait(BAR(C::B_FULL + sl), (i / C::NSLOT) & 1, ab)) return false;
         const uint32_t vs = sbase + C::OFF_RING + sl * C::TB;
         for (int x = 0; x < 2; ++x) {
           if (!use[x]) continue;
-          if (!mbar_wait(BAR(C::B_PFULL + x), npv[x] & 1, ab)) return false;
+          if (!warp_wait(BAR(C::B_PFULL + x), npv[x] & 1, ab)) return false;
           tc_fence_after();
           const uint32_t ps = sbase + C::OFF_P + x * C::P_BYTES;
 #pragma unroll
           for (int kk = 0; kk < kTile / 16; ++kk) {
             const uint64_t a = sdesc(ps + (kk >> 2) * kTile * 128 + (kk & 3) * 32, 16, 1024);
             const uint64_t bd = sdesc(vs + kk * 16 * 128, kTile * 128, 1024);
-            mma_ss(tmem + C::COL_O + x * D, a, bd, ID_O, (npv[x] > 0 || kk > 0) ? 1u : 0u);
+            mma_ss_w(tmem + C::COL_O + x * D, a, bd, ID_O, (npv[x] > 0 || kk > 0) ? 1u : 0u);
           }
-          mma_commit(BAR(C::B_PVDONE + x));
+          mma_commit_w(BAR(C::B_PVDONE + x));
           ++npv[x];
         }
-        mma_commit(BAR(C::B_EMPTY + sl));
+        mma_commit_w(BAR(C::B_EMPTY + sl));
         return true;
       };
       for (int j = 0; ok && j < sch.ntiles; ++j) {
@@ -176,30 +176,30 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
         bool g, use[2];
         sch.tile(j, row0, g, use[0], use[1]);
         const int i = 2 * j, sl = i % C::NSLOT;
-        if (!mbar_wait(BAR(C::B_FULL + sl), (i / C::NSLOT) & 1, ab)) { ok = false; break; }
+        if (!warp_wait(BAR(C::B_FULL + sl), (i / C::NSLOT) & 1, ab)) { ok = false; break; }
         const uint32_t ks = sbase + C::OFF_RING + sl * C::TB;
         for (int x = 0; x < 2 && ok; ++x) {
           if (!use[x]) continue;
-          if (ns[x] > 0 && !mbar_wait(BAR(C::B_SFREE + x), (ns[x] - 1) & 1, ab)) { ok = false; break; }
+          if (ns[x] > 0 && !warp_wait(BAR(C::B_SFREE + x), (ns[x] - 1) & 1, ab)) { ok = false; break; }
           tc_fence_after();
           const uint32_t qs = sbase + C::OFF_Q + x * C::TB;
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off = (kk >> 2) * kTile * 128 + (kk & 3) * 32;
-            mma_ss(tmem + C::COL_S + x * kTile, sdesc(qs + off, 16, 1024), sdesc(ks + off, 16, 1024), ID_S,
+            mma_ss_w(tmem + C::COL_S + x * kTile, sdesc(qs + off, 16, 1024), sdesc(ks + off, 16, 1024), ID_S,
                    kk > 0 ? 1u : 0u);
           }
-          mma_commit(BAR(C::B_SFULL + x));
+          mma_commit_w(BAR(C::B_SFULL + x));
           ++ns[x];
         }
         if (!ok) break;
-        mma_commit(BAR(C::B_EMPTY + sl));
+        mma_commit_w(BAR(C::B_EMPTY + sl));
         if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
       }
       if (ok) ok = issue_pv(sch.ntiles - 1);
       if (!ok) {
         // aborting: let every MMA already issued finish before TMEM is freed
-        mma_commit(BAR(C::B_DRAIN));
+        mma_commit_w(BAR(C::B_DRAIN));
         mbar_wait_bounded(BAR(C::B_DRAIN), 0);
       }
     }
