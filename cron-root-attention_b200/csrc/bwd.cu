@@ -92,17 +92,22 @@ __global__ void __launch_bounds__(256) delta_kernel(const void* __restrict__ op,
 // ===========================================================================
 // Optional cycle counters of the dQ pass (build with -DCRA_PROF; read with
 // cra_dq_prof): per role, cycles spent waiting on each barrier and working.
+// Counters live in registers and are flushed once per warp at exit.
 #ifdef CRA_PROF
 __device__ unsigned long long g_dq_prof[32];
+#define PROF_DECL unsigned long long pacc[32] = {};
 #define PROF_T(v) const unsigned long long v = clock64()
-#define PROF_ADD(k, t0) \
-  if ((threadIdx.x & 31) == 0) atomicAdd(&g_dq_prof[k], clock64() - (t0))
-#define PROF_CNT(k, n) \
-  if ((threadIdx.x & 31) == 0) atomicAdd(&g_dq_prof[k], static_cast<unsigned long long>(n))
+#define PROF_ADD(k, t0) (pacc[k] += clock64() - (t0))
+#define PROF_CNT(k, n) (pacc[k] += static_cast<unsigned long long>(n))
+#define PROF_FLUSH()                                                     \
+  if ((threadIdx.x & 31) == 0)                                           \
+    _Pragma("unroll") for (int k = 0; k < 32; ++k) if (pacc[k]) atomicAdd(&g_dq_prof[k], pacc[k]);
 #else
+#define PROF_DECL
 #define PROF_T(v)
 #define PROF_ADD(k, t0)
 #define PROF_CNT(k, n)
+#define PROF_FLUSH()
 #endif
 
 struct DqUnits {
@@ -180,6 +185,7 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
   const Abort ab{abort_flag, p.err};
+  PROF_DECL
 
   if (threadIdx.x == 0) {
     mbar_init(BAR(C::B_QFULL), 1);
@@ -377,9 +383,7 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
             ok = false;
             break;
           }
-#ifdef CRA_PROF
-          if (lane == 0) PROF_ADD(12, t0);
-#endif
+          PROF_ADD(12, t0);
           PROF_T(t1);
           tc_fence_after();
           int lo, hi;
@@ -410,9 +414,7 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
           tmem_st_wait();
           tc_fence_before();
           mbar_arrive(BAR(C::B_DSFULL + w));
-#ifdef CRA_PROF
-          if (lane == 0) PROF_ADD(13, t1);
-#endif
+          PROF_ADD(13, t1);
         }
     }
   } else {
@@ -424,9 +426,7 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
       const int acc = it & 1;
       PROF_T(t0);
       if (!mbar_wait(BAR(C::B_ACCFULL + acc), (it >> 1) & 1, ab)) break;
-#ifdef CRA_PROF
-      if (lane == 0) PROF_ADD(16, t0);
-#endif
+      PROF_ADD(16, t0);
       tc_fence_after();
       uint32_t pk[D / 2];
 #pragma unroll
@@ -449,6 +449,7 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
       }
     }
   }
+  PROF_FLUSH()
   tc_fence_before();
   __syncthreads();
   tc_fence_after();

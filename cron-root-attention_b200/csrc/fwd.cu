@@ -12,15 +12,21 @@
 //   warp 0      TMA producer: Q_A, Q_B once, then K_j, V_j, K_j+1, ... into a
 //               ring of NSLOT 128-row slots (K and V tiles are separate
 //               ring entries).
-//   warp 1      tcgen05 issuer (one thread) + TMEM owner.  Per key tile j:
-//               S_A = Q_A K_j^T, S_B = Q_B K_j^T (each only if that tile
-//               needs K_j), then O_A += P_A V_{j-1}, O_B += P_B V_{j-1}.
+//   warp 1      tcgen05 issuer (whole warp, one elected lane) + TMEM owner.
+//               Per key tile j and query tile x in {A, B} that needs it:
+//               O_x += P_x V_{j'} for x's previous key tile j', then
+//               S_x = Q_x K_j^T.
 //   warps 2-5   softmax of tile A, warps 6-9 softmax of tile B: a thread owns
 //               one query row (TMEM lane = 32 * (warp % 4) + lane).  It loads
 //               its score row, masks it with per-row [lo, hi) column bounds,
-//               updates the running max / sum and writes P (bf16 / f16,
-//               swizzled) to shared memory.  O is rescaled in TMEM only when
-//               the running max grows by more than 2^8 (exact either way).
+//               updates the running max / sum and writes P (16-bit) back into
+//               TMEM over the scores; P V is a TS-form MMA (A from TMEM).  O
+//               is rescaled in TMEM only when the running max grows by more
+//               than 2^8 (exact either way).
+// TMEM holds S/P and O of both tiles (4 x 128 columns for D = 128).  A tile's
+// next scores are issued after its PV product, so MMA issue order protects
+// P, and the commit that signals "scores ready" also covers every earlier PV
+// product: when the softmax sees S_x(n), O_x holds all of P_x V up to n - 1.
 // A CTA may also work on one GPU's shard of a sequence split across GPUs:
 // queries [q_begin, q_begin + q_len) with K / V rows from kv_begin (a W - 1
 // row halo before the shard) and the full global-row list.
@@ -32,28 +38,43 @@
 
 namespace cra {
 
+// Optional cycle counters (build with -DCRA_PROF; read with cra_fwd_prof).
+#ifdef CRA_PROF
+__device__ unsigned long long g_fwd_prof[32];
+#define FPROF_DECL unsigned long long pacc[32] = {};
+#define FPROF_T(v) const unsigned long long v = clock64()
+#define FPROF_ADD(k, t0) (pacc[k] += clock64() - (t0))
+#define FPROF_CNT(k, n) (pacc[k] += static_cast<unsigned long long>(n))
+#define FPROF_FLUSH()                                                    \
+  if ((threadIdx.x & 31) == 0)                                           \
+    _Pragma("unroll") for (int k = 0; k < 32; ++k) if (pacc[k]) atomicAdd(&g_fwd_prof[k], pacc[k]);
+#else
+#define FPROF_DECL
+#define FPROF_T(v)
+#define FPROF_ADD(k, t0)
+#define FPROF_CNT(k, n)
+#define FPROF_FLUSH()
+#endif
+
 template <int D>
 struct FwdCfg {
   static constexpr int TB = kTile * D * 2;            // one [128 x D] tile
-  static constexpr int NSLOT = (D == 128) ? 3 : 6;    // K/V ring slots
-  static constexpr int P_BYTES = kTile * kTile * 2;
+  static constexpr int NSLOT = (D == 128) ? 5 : 12;   // K/V ring slots
   static constexpr int OFF_Q = 0;                      // Q_A, Q_B
-  static constexpr int OFF_P = OFF_Q + 2 * TB;         // P_A, P_B
-  static constexpr int OFF_RING = OFF_P + 2 * P_BYTES;
+  static constexpr int OFF_RING = OFF_Q + 2 * TB;
   static constexpr int OFF_BAR = OFF_RING + NSLOT * TB;
   static constexpr int B_QFULL = 0;
   static constexpr int B_FULL = 1;                     // [NSLOT]
   static constexpr int B_EMPTY = B_FULL + NSLOT;       // [NSLOT]
   static constexpr int B_SFULL = B_EMPTY + NSLOT;      // [2] per query tile
-  static constexpr int B_SFREE = B_SFULL + 2;          // [2]
-  static constexpr int B_PFULL = B_SFREE + 2;          // [2]
-  static constexpr int B_PVDONE = B_PFULL + 2;         // [2]
-  static constexpr int B_DRAIN = B_PVDONE + 2;
+  static constexpr int B_PFULL = B_SFULL + 2;          // [2]
+  static constexpr int B_ODONE = B_PFULL + 2;          // [2] all PV products of a tile done
+  static constexpr int B_DRAIN = B_ODONE + 2;
   static constexpr int N_BAR = B_DRAIN + 1;
   static constexpr int OFF_MISC = OFF_BAR + N_BAR * 8;  // tmem slot, abort flag
   static constexpr int SMEM = OFF_MISC + 16 + 1024;     // + alignment slack
   static constexpr int TMEM_COLS = 512;
-  // TMEM columns: S_A, S_B (128 each), then O_A, O_B (D each)
+  // TMEM columns: S_A, S_B (128 each; P over the first 64), then O_A, O_B (D each)
   static constexpr int COL_S = 0, COL_O = 256;
   static_assert(SMEM <= 232448, "shared memory budget");
 };
@@ -79,6 +100,7 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
   const Abort ab{abort_flag, p.err};
+  FPROF_DECL
 
   if (threadIdx.x == 0) {
     mbar_init(BAR(C::B_QFULL), 1);
@@ -88,9 +110,8 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(BAR(C::B_SFULL + x), 1);
-      mbar_init(BAR(C::B_SFREE + x), 128);
       mbar_init(BAR(C::B_PFULL + x), 128);
-      mbar_init(BAR(C::B_PVDONE + x), 1);
+      mbar_init(BAR(C::B_ODONE + x), 1);
     }
     mbar_init(BAR(C::B_DRAIN), 1);
     *abort_flag = 0;
@@ -144,59 +165,62 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
     {  // whole warp, converged; one elected lane issues
       constexpr uint32_t ID_S = idesc_f16(BF16, kTile, kTile, false, false);
       constexpr uint32_t ID_O = idesc_f16(BF16, kTile, D, false, true);
+      FPROF_T(tstart);
       bool ok = warp_wait(BAR(C::B_QFULL), 0, ab);
-      int ns[2] = {0, 0};   // score tiles issued per query tile
-      int npv[2] = {0, 0};  // PV products issued per query tile
-      auto issue_pv = [&](int j) -> bool {
-        int row0;
-        bool g, use[2];
-        sch.tile(j, row0, g, use[0], use[1]);
-        const int i = 2 * j + 1, sl = i % C::NSLOT;
-        if (!warp_wait(BAR(C::B_FULL + sl), (i / C::NSLOT) & 1, ab)) return false;
-        const uint32_t vs = sbase + C::OFF_RING + sl * C::TB;
-        for (int x = 0; x < 2; ++x) {
-          if (!use[x]) continue;
-          if (!warp_wait(BAR(C::B_PFULL + x), npv[x] & 1, ab)) return false;
-          tc_fence_after();
-          const uint32_t ps = sbase + C::OFF_P + x * C::P_BYTES;
+      FPROF_ADD(3, tstart);
+      const uint64_t qdesc[2] = {sdesc(sbase + C::OFF_Q, 16, 1024), sdesc(sbase + C::OFF_Q + C::TB, 16, 1024)};
+      int ns[2] = {0, 0};      // score tiles issued per query tile
+      int pend[2] = {-1, -1};  // key tile whose PV product is still to issue
+      auto full = [&](int i) { return warp_wait(BAR(C::B_FULL + i % C::NSLOT), (i / C::NSLOT) & 1, ab); };
+      // O_x += P_x V_jp  (P from TMEM over S_x; V_jp is ring entry 2 jp + 1)
+      auto issue_pv = [&](int x) -> bool {
+        const int jp = pend[x], i = 2 * jp + 1;
+        FPROF_T(t0);
+        if (!warp_wait(BAR(C::B_PFULL + x), (ns[x] - 1) & 1, ab)) return false;
+        FPROF_ADD(1, t0);
+        FPROF_T(t1);
+        if (!full(i)) return false;
+        FPROF_ADD(2, t1);
+        tc_fence_after();
+        const uint64_t vd = sdesc(sbase + C::OFF_RING + (i % C::NSLOT) * C::TB, kTile * 128, 1024);
 #pragma unroll
-          for (int kk = 0; kk < kTile / 16; ++kk) {
-            const uint64_t a = sdesc(ps + (kk >> 2) * kTile * 128 + (kk & 3) * 32, 16, 1024);
-            const uint64_t bd = sdesc(vs + kk * 16 * 128, kTile * 128, 1024);
-            mma_ss_w(tmem + C::COL_O + x * D, a, bd, ID_O, (npv[x] > 0 || kk > 0) ? 1u : 0u);
-          }
-          mma_commit_w(BAR(C::B_PVDONE + x));
-          ++npv[x];
-        }
-        mma_commit_w(BAR(C::B_EMPTY + sl));
+        for (int kk = 0; kk < kTile / 16; ++kk)
+          mma_ts_w(tmem + C::COL_O + x * D, tmem + C::COL_S + x * kTile + kk * 8, vd + ((kk * 16 * 128) >> 4), ID_O,
+                   (ns[x] > 1 || kk > 0) ? 1u : 0u);
+        pend[x] = -1;
         return true;
       };
-      for (int j = 0; ok && j < sch.ntiles; ++j) {
-        int row0;
-        bool g, use[2];
-        sch.tile(j, row0, g, use[0], use[1]);
-        const int i = 2 * j, sl = i % C::NSLOT;
-        if (!warp_wait(BAR(C::B_FULL + sl), (i / C::NSLOT) & 1, ab)) { ok = false; break; }
-        const uint32_t ks = sbase + C::OFF_RING + sl * C::TB;
+      for (int j = 0; ok && j <= sch.ntiles; ++j) {
+        int row0 = 0;
+        bool g = false, use[2] = {false, false};
+        if (j < sch.ntiles) sch.tile(j, row0, g, use[0], use[1]);
         for (int x = 0; x < 2 && ok; ++x) {
+          if (pend[x] >= 0 && !issue_pv(x)) { ok = false; break; }
           if (!use[x]) continue;
-          if (ns[x] > 0 && !warp_wait(BAR(C::B_SFREE + x), (ns[x] - 1) & 1, ab)) { ok = false; break; }
+          FPROF_T(t0);
+          if (!full(2 * j)) { ok = false; break; }
+          FPROF_ADD(2, t0);
           tc_fence_after();
-          const uint32_t qs = sbase + C::OFF_Q + x * C::TB;
+          const uint64_t kd = sdesc(sbase + C::OFF_RING + ((2 * j) % C::NSLOT) * C::TB, 16, 1024);
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kTile * 128 + (kk & 3) * 32;
-            mma_ss_w(tmem + C::COL_S + x * kTile, sdesc(qs + off, 16, 1024), sdesc(ks + off, 16, 1024), ID_S,
-                   kk > 0 ? 1u : 0u);
+            const uint32_t off = ((kk >> 2) * kTile * 128 + (kk & 3) * 32) >> 4;
+            mma_ss_w(tmem + C::COL_S + x * kTile, qdesc[x] + off, kd + off, ID_S, kk > 0 ? 1u : 0u);
           }
           mma_commit_w(BAR(C::B_SFULL + x));
           ++ns[x];
+          pend[x] = j;
         }
         if (!ok) break;
-        mma_commit_w(BAR(C::B_EMPTY + sl));
-        if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
+        if (j > 0) mma_commit_w(BAR(C::B_EMPTY + (2 * j - 1) % C::NSLOT));  // V_{j-1}: both PV products issued
+        if (j < sch.ntiles) mma_commit_w(BAR(C::B_EMPTY + (2 * j) % C::NSLOT));  // K_j: both score tiles issued
       }
-      if (ok) ok = issue_pv(sch.ntiles - 1);
+      if (ok)
+        for (int x = 0; x < 2; ++x)
+          if (ns[x] > 0) mma_commit_w(BAR(C::B_ODONE + x));
+      FPROF_ADD(0, tstart);
+      FPROF_CNT(30, ns[0] + ns[1]);
+      FPROF_CNT(31, 1);
       if (!ok) {
         // aborting: let every MMA already issued finish before TMEM is freed
         mma_commit_w(BAR(C::B_DRAIN));
@@ -225,14 +249,17 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
       bool g, ua, ub;
       sch.tile(j, row0, g, ua, ub);
       if (!(x == 0 ? ua : ub)) continue;
+      FPROF_T(tw);
       if (!mbar_wait(BAR(C::B_SFULL + x), n & 1, ab)) { ok = false; break; }
+      FPROF_ADD(8, tw);
+      FPROF_T(tl);
       tc_fence_after();
       float s[4][32];
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(scol + 32 * c, s[c]);
       tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(BAR(C::B_SFREE + x));
+      FPROF_ADD(9, tl);
+      FPROF_T(tc);
       int lo, hi;
       if (!g) {
         lo = ls - row0;
@@ -244,22 +271,33 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
       if (!row_ok) { lo = 0; hi = 0; }
       lo = max(lo, 0);
       hi = min(hi, kTile);
-      float mx = -INFINITY;
-      if (lo == 0 && hi == kTile) {
+      if (__any_sync(0xffffffffu, lo != 0 || hi != kTile)) {
+        // visible columns [lo, hi) as one 32-bit mask per 32-column chunk
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < 4; ++c) {
+          const int a = min(max(lo - 32 * c, 0), 32), z = min(max(hi - 32 * c, 0), 32);
+          const uint32_t mz = z >= 32 ? 0xffffffffu : ((1u << z) - 1u);
+          const uint32_t ma = a >= 32 ? 0xffffffffu : ((1u << a) - 1u);
+          const uint32_t m = mz & ~ma;
 #pragma unroll
-          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, s[c][e]);
-      } else {
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int col = 32 * c + e;
-            s[c][e] = (col >= lo && col < hi) ? s[c][e] : -INFINITY;
-            mx = fmaxf(mx, s[c][e]);
-          }
+          for (int e = 0; e < 32; ++e) s[c][e] = (m & (1u << e)) ? s[c][e] : -INFINITY;
+        }
       }
+      // row max with 8 independent partial maxima (short dependency chains)
+      float pm0 = s[0][0], pm1 = s[0][1], pm2 = s[0][2], pm3 = s[0][3];
+      float pm4 = s[0][4], pm5 = s[0][5], pm6 = s[0][6], pm7 = s[0][7];
+#pragma unroll
+      for (int k = 1; k < 16; ++k) {
+        pm0 = fmaxf(pm0, s[k >> 2][8 * (k & 3) + 0]);
+        pm1 = fmaxf(pm1, s[k >> 2][8 * (k & 3) + 1]);
+        pm2 = fmaxf(pm2, s[k >> 2][8 * (k & 3) + 2]);
+        pm3 = fmaxf(pm3, s[k >> 2][8 * (k & 3) + 3]);
+        pm4 = fmaxf(pm4, s[k >> 2][8 * (k & 3) + 4]);
+        pm5 = fmaxf(pm5, s[k >> 2][8 * (k & 3) + 5]);
+        pm6 = fmaxf(pm6, s[k >> 2][8 * (k & 3) + 6]);
+        pm7 = fmaxf(pm7, s[k >> 2][8 * (k & 3) + 7]);
+      }
+      float mx = fmaxf(fmaxf(fmaxf(pm0, pm1), fmaxf(pm2, pm3)), fmaxf(fmaxf(pm4, pm5), fmaxf(pm6, pm7)));
       mx *= sl;
       const bool need = mx > m_run + 8.0f;  // false while the row has seen nothing
       const bool any = __any_sync(0xffffffffu, need);
@@ -269,49 +307,53 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
         m_run = mx;
       }
       const float mu = (m_run == -INFINITY) ? 0.f : m_run;
-      float sum = 0.f;
+      FPROF_ADD(10, tc);
+      FPROF_T(tp);
+      // P = 2^(s * scale_log2 - m), written as 16-bit pairs over score
+      // columns [0, 64) of this tile.
+      const float nmu = -mu;
+      float q0 = 0.f, q1 = 0.f, q2 = 0.f, q3 = 0.f;  // partial row sums
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          s[c][e] = ex2(fmaf(s[c][e], sl, -mu));
-          sum += s[c][e];
+        for (int e = 0; e < 32; e += 2) {
+          float a0 = s[c][e], a1 = s[c][e + 1];
+          ffma2(a0, a1, sl, nmu);
+          a0 = ex2(a0);
+          a1 = ex2(a1);
+          if (e & 2)
+            fadd2(q2, q3, a0, a1);
+          else
+            fadd2(q0, q1, a0, a1);
+          pk[e / 2] = E::pack(a0, a1);
         }
-      l_run = l_run * factor + sum;
-      if (n > 0) {
-        if (!mbar_wait(BAR(C::B_PVDONE + x), (n - 1) & 1, ab)) { ok = false; break; }
-        tc_fence_after();
-        if (any) {
+        tmem_st16(scol + 16 * c, pk);
+      }
+      l_run = l_run * factor + ((q0 + q1) + (q2 + q3));
+      // Rescale O (after P, when the scores are dead).  O_x already holds
+      // every PV product up to key tile n - 1: the commit that signalled
+      // these scores also covers them.
+      if (n > 0 && any) {
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            float o[32];
-            tmem_ld32(ocol + 32 * c, o);
-            tmem_ld_wait();
+        for (int c = 0; c < D / 32; ++c) {
+          float o[32];
+          tmem_ld32(ocol + 32 * c, o);
+          tmem_ld_wait();
 #pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] *= factor;
-            tmem_st32(ocol + 32 * c, o);
-          }
-          tmem_st_wait();
+          for (int e = 0; e < 32; ++e) o[e] *= factor;
+          tmem_st32(ocol + 32 * c, o);
         }
       }
-      uint8_t* prow = smem + C::OFF_P + x * C::P_BYTES;
-#pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        const int c = u >> 2, e0 = (u & 3) * 8;
-        uint4 pk;
-        pk.x = E::pack(s[c][e0 + 0], s[c][e0 + 1]);
-        pk.y = E::pack(s[c][e0 + 2], s[c][e0 + 3]);
-        pk.z = E::pack(s[c][e0 + 4], s[c][e0 + 5]);
-        pk.w = E::pack(s[c][e0 + 6], s[c][e0 + 7]);
-        *reinterpret_cast<uint4*>(prow + sw128_off(r, u, kTile)) = pk;
-      }
-      fence_proxy_async_smem();
+      tmem_st_wait();
       tc_fence_before();
       mbar_arrive(BAR(C::B_PFULL + x));
+      FPROF_ADD(11, tp);
+      FPROF_CNT(12, any ? 1 : 0);
       ++n;
     }
     // ---------------------------------------------------------- epilogue
-    if (tile_ok && ok && n > 0 && mbar_wait(BAR(C::B_PVDONE + x), (n - 1) & 1, ab)) {
+    if (tile_ok && ok && n > 0 && mbar_wait(BAR(C::B_ODONE + x), 0, ab)) {
       tc_fence_after();
       const float inv = 1.f / fmaxf(l_run, 1e-6f);
       typename E::T* orow = reinterpret_cast<typename E::T*>(p.out) + b * p.out_sb + h * p.out_sh +
@@ -339,11 +381,23 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
     }
   }
 
+  FPROF_FLUSH()
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
 }
+
+#ifdef CRA_PROF
+extern "C" __attribute__((visibility("default"))) int cra_fwd_prof(unsigned long long* out32, int reset) {
+  cudaMemcpyFromSymbol(out32, g_fwd_prof, sizeof(g_fwd_prof));
+  if (reset) {
+    unsigned long long z[32] = {};
+    cudaMemcpyToSymbol(g_fwd_prof, z, sizeof(z));
+  }
+  return 0;
+}
+#endif
 
 template <int D, bool BF16>
 static cudaError_t launch_fwd_t(const QueryPassParams& p, cudaStream_t stream) {

@@ -306,24 +306,16 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// 2^x on the FMA pipe, for softmax weights that are rounded to 16 bits
-// afterwards (relieves the MUFU unit, which runs at a quarter of the FMA
-// rate).  Range reduction: n = round-to-nearest(x) by adding 1.5 * 2^23, so
-// f = x - n lies in [-1/2, 1/2]; 2^f is a degree-3 polynomial whose
-// coefficients were fitted here by relative-error-weighted least squares on
-// Chebyshev nodes of [-1/2, 1/2] (max relative error 7.5e-5 in fp32 Horner
-// evaluation, below half an ulp of fp16 and bf16); 2^n is added into the
-// exponent field.  x is clamped to >= -125 so the exponent never underflows;
-// the result for x <= -125 is ~2^-125 instead of 0 (negligible next to any
-// visible weight, and masked entries are zeroed by the callers).
-__device__ __forceinline__ float ex2_poly(float x) {
-  x = fmaxf(x, -125.f);
-  const float t = x + 12582912.f;  // 1.5 * 2^23: low mantissa bits hold n
-  const float f = x - (t - 12582912.f);
-  float p = fmaf(f, 0.055172745138406754f, 0.24261125922203064f);
-  p = fmaf(p, f, 0.6932607889175415f);
-  p = fmaf(p, f, 0.9999280571937561f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+// 32 lanes x 32 columns of 32-bit raw words.
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%"
+      "19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
 }
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
