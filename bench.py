@@ -272,7 +272,7 @@ def run_ours(args, rank, world, local_rank):
     # DRAM bytes per forward launch: ncu dram__bytes_read.sum + write.sum of one
     # launch at H = 8 (profiles/kernels_northstar_h8.md: 405.9 + 117.1 MB),
     # scaled by H / 8 (the traffic grows in proportion to the heads)
-    traffic = (405.864704e6 + 117.078272e6) * (H / 8) if (S, D) == (65536, 128) else None
+    traffic = (405.935360e6 + 119.967488e6) * (H / 8) if (S, D) == (65536, 128) else None
     line = {
         "metric": METRIC,
         "value": world * (f_fwd + f_bwd) / (ms_step * 1e-3) / 1e12,
