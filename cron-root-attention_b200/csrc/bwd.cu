@@ -807,6 +807,345 @@ __global__ void __launch_bounds__(320, 1) keypass_kernel(const __grid_constant__
 }
 
 // ===========================================================================
+// Local key pass, persistent.  One CTA per SM walks the local key tiles t =
+// blockIdx.x, blockIdx.x + gridDim.x, ... (kt fastest, latest keys first).
+// Per tile the work is the key-centric pass above in LOCAL mode; across tiles
+//   * K / V are double-buffered (tile i in buffer i & 1), so the next tile's
+//     K / V arrive while the current tile runs;
+//   * the Q / dO unit stream, the MMA issue and the two softmax warpgroups
+//     run on without a break (one global unit counter);
+//   * a dedicated epilogue warpgroup drains dK / dV (plus the dG fold-in) of
+//     tile i while tile i + 1 starts; only tile i + 1's first dV / dK product
+//     waits for it (ACCFREE).
+// Warps: 0 producer, 1 MMA issuer, 2-5 / 6-9 softmax, 10-13 epilogue.
+// ===========================================================================
+template <int D>
+struct KeyLocalCfg {
+  static constexpr int TB = kTile * D * 2;         // K or V tile
+  static constexpr int UB = kUnit * D * 2;         // Q or dO unit
+  static constexpr int NSQ = (D == 128) ? 3 : 8;   // Q/dO unit stages
+  static constexpr int OFF_KV = 0;                 // buffer b: K at 2 b TB, V at (2 b + 1) TB
+  static constexpr int OFF_Q = 4 * TB;             // stage s: Q at OFF_Q + 2 s UB, dO after it
+  static constexpr int OFF_LSE = OFF_Q + NSQ * 2 * UB;  // stage s: lse2[64], delta[64]
+  static constexpr int OFF_BAR = OFF_LSE + NSQ * 2 * kUnit * 4;
+  static constexpr int B_KVFULL = 0, B_KVEMPTY = 2, B_QFULL = 4, B_QEMPTY = 4 + NSQ, B_SFULL = 4 + 2 * NSQ,
+                       B_PFULL = B_SFULL + 2, B_ACCFULL = B_PFULL + 2, B_ACCFREE = B_ACCFULL + 1,
+                       B_DRAIN = B_ACCFREE + 1, N_BAR = B_DRAIN + 1;
+  static constexpr int OFF_MISC = OFF_BAR + N_BAR * 8;
+  static constexpr int SMEM = OFF_MISC + 16 + 1024;
+  static constexpr int COL_DV = 256, COL_DK = 256 + D;  // slots at 0 and 128 as in KeyCfg
+  static constexpr int THREADS = 448;
+  static_assert(SMEM <= 232448, "shared memory budget");
+};
+
+// Local key tile t of the persistent walk and the 64-query units it meets.
+struct KeyLocalTile {
+  int k0, hk, b, t_lo, nT, nU;
+  __device__ __forceinline__ KeyLocalTile(int t, int n_ktiles, int Hkv, int S, int W, int groups) {
+    const int kt = t % n_ktiles;
+    hk = (t / n_ktiles) % Hkv;
+    b = t / (n_ktiles * Hkv);
+    k0 = (n_ktiles - 1 - kt) * kTile;
+    const int qlast = min(k0 + kTile - 1 + W - 1, S - 1);
+    t_lo = k0 / kUnit;
+    nT = qlast / kUnit + 1 - t_lo;
+    nU = nT * groups;
+  }
+  __device__ __forceinline__ void unit(int ul, int groups, int& h, int& q0) const {
+    h = hk * groups + ul / nT;
+    q0 = (t_lo + ul % nT) * kUnit;
+  }
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant__ KeyPassParams p) {
+  using C = KeyLocalCfg<D>;
+  using E = Elt<BF16>;
+  using T = typename E::T;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int W = p.W, S = p.S, R = p.R;
+  const int Spad = ((S + kTile - 1) / kTile) * kTile;
+  const int groups = p.kv_groups;
+  const int Hkv = p.H / groups;
+  const int n_tiles = p.n_ktiles * Hkv * p.B;
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + C::OFF_BAR;
+  auto BAR = [&](int i) { return bar0 + 8u * i; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+  const Abort ab{abort_flag, p.err};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(BAR(C::B_KVFULL + s), 1);
+      mbar_init(BAR(C::B_KVEMPTY + s), 1);
+      mbar_init(BAR(C::B_SFULL + s), 1);
+      mbar_init(BAR(C::B_PFULL + s), 128);
+    }
+    for (int i = 0; i < C::NSQ; ++i) {
+      mbar_init(BAR(C::B_QFULL + i), 1);
+      mbar_init(BAR(C::B_QEMPTY + i), 1);
+    }
+    mbar_init(BAR(C::B_ACCFULL), 1);
+    mbar_init(BAR(C::B_ACCFREE), 128);
+    mbar_init(BAR(C::B_DRAIN), 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(smem_u32(tmem_slot), 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      int e = 0, nkv = 0;  // Q/dO units issued, K/V tiles issued
+      bool ok = true;
+      for (int t = blockIdx.x, i = 0; ok && t < n_tiles; t += gridDim.x, ++i) {
+        const KeyLocalTile tl(t, p.n_ktiles, Hkv, S, W, groups);
+        const int kb = i & 1;
+        if (i >= 2 && !mbar_wait(BAR(C::B_KVEMPTY + kb), ((i >> 1) - 1) & 1, ab)) break;
+        mbar_expect_tx(BAR(C::B_KVFULL + kb), 2 * C::TB);
+        const uint32_t kd = sbase + C::OFF_KV + 2 * kb * C::TB;
+        for (int c = 0; c < D / 64; ++c) {
+          tma_load_4d(kd + c * kTile * 128, &p.tm_k, BAR(C::B_KVFULL + kb), c * 64, tl.k0, tl.hk, tl.b);
+          tma_load_4d(kd + C::TB + c * kTile * 128, &p.tm_v, BAR(C::B_KVFULL + kb), c * 64, tl.k0, tl.hk, tl.b);
+        }
+        ++nkv;
+        for (int ul = 0; ul < tl.nU; ++ul, ++e) {
+          const int st = e % C::NSQ;
+          if (e >= C::NSQ && !mbar_wait(BAR(C::B_QEMPTY + st), ((e / C::NSQ) - 1) & 1, ab)) { ok = false; break; }
+          int h, q0;
+          tl.unit(ul, groups, h, q0);
+          const uint32_t qd = sbase + C::OFF_Q + st * 2 * C::UB;
+          mbar_expect_tx(BAR(C::B_QFULL + st), 2 * C::UB + 2 * kUnit * 4);
+          for (int c = 0; c < D / 64; ++c) {
+            tma_load_4d(qd + c * kUnit * 128, &p.tm_q, BAR(C::B_QFULL + st), c * 64, q0, h, tl.b);
+            tma_load_4d(qd + C::UB + c * kUnit * 128, &p.tm_do, BAR(C::B_QFULL + st), c * 64, q0, h, tl.b);
+          }
+          const int64_t li = (static_cast<int64_t>(tl.b) * p.H + h) * Spad + q0;
+          const uint32_t ld = sbase + C::OFF_LSE + st * 2 * kUnit * 4;
+          bulk_load(ld, p.lse + li, kUnit * 4, BAR(C::B_QFULL + st));
+          bulk_load(ld + kUnit * 4, p.delta + li, kUnit * 4, BAR(C::B_QFULL + st));
+        }
+      }
+      if (*abort_flag) {  // let copies in flight land before the CTA exits
+        for (int u = (e > C::NSQ ? e - C::NSQ : 0); u < e; ++u)
+          mbar_wait_bounded(BAR(C::B_QFULL + u % C::NSQ), (u / C::NSQ) & 1);
+        for (int i = (nkv > 2 ? nkv - 2 : 0); i < nkv; ++i) mbar_wait_bounded(BAR(C::B_KVFULL + (i & 1)), (i >> 1) & 1);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (whole warp, one elected lane) ----------------
+    constexpr uint32_t ID_S = idesc_f16(BF16, kTile, kUnit, false, false);
+    constexpr uint32_t ID_G = idesc_f16(BF16, kTile, D, false, true);
+    bool ok = true;
+    // dV += P^T dO, dK += dS^T Q for unit i (of tile iteration iti)
+    auto issue_kv = [&](int i, int iti, bool first, bool last) -> bool {
+      const int st = i % C::NSQ, sl = i & 1;
+      if (!warp_wait(BAR(C::B_PFULL + sl), (i >> 1) & 1, ab)) return false;
+      if (first && iti >= 1 && !warp_wait(BAR(C::B_ACCFREE), (iti - 1) & 1, ab)) return false;
+      tc_fence_after();
+      const uint32_t qd = sbase + C::OFF_Q + st * 2 * C::UB;
+      const uint64_t dod = sdesc(qd + C::UB, kUnit * 128, 1024), qdd = sdesc(qd, kUnit * 128, 1024);
+#pragma unroll
+      for (int kk = 0; kk < kUnit / 16; ++kk) {
+        const uint32_t boff = (kk * 16 * 128) >> 4;
+        mma_ts_w(tmem + C::COL_DV, tmem + 128 * sl + kk * 8, dod + boff, ID_G, (!first || kk > 0) ? 1u : 0u);
+        mma_ts_w(tmem + C::COL_DK, tmem + 128 * sl + 64 + kk * 8, qdd + boff, ID_G, (!first || kk > 0) ? 1u : 0u);
+      }
+      mma_commit_w(BAR(C::B_QEMPTY + st));
+      if (last) mma_commit_w(BAR(C::B_ACCFULL));
+      return true;
+    };
+    int u = 0, pit = -1;
+    bool pfirst = false;
+    for (int t = blockIdx.x, i = 0; ok && t < n_tiles; t += gridDim.x, ++i) {
+      const KeyLocalTile tl(t, p.n_ktiles, Hkv, S, W, groups);
+      const int kb = i & 1;
+      if (!warp_wait(BAR(C::B_KVFULL + kb), (i >> 1) & 1, ab)) { ok = false; break; }
+      const uint64_t kd = sdesc(sbase + C::OFF_KV + 2 * kb * C::TB, 16, 1024);
+      const uint64_t vd = sdesc(sbase + C::OFF_KV + (2 * kb + 1) * C::TB, 16, 1024);
+      for (int ul = 0; ul < tl.nU; ++ul, ++u) {
+        const int st = u % C::NSQ, sl = u & 1;
+        // slot sl was last read by the dV / dK products of unit u - 2, issued
+        // before this S^T / dP^T (in-order execution)
+        if (!warp_wait(BAR(C::B_QFULL + st), (u / C::NSQ) & 1, ab)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t qa = sbase + C::OFF_Q + st * 2 * C::UB;
+        const uint64_t qd = sdesc(qa, 16, 1024), dd = sdesc(qa + C::UB, 16, 1024);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t ko = ((kk >> 2) * kTile * 128 + (kk & 3) * 32) >> 4;
+          const uint32_t qo = ((kk >> 2) * kUnit * 128 + (kk & 3) * 32) >> 4;
+          mma_ss_w(tmem + 128 * sl, kd + ko, qd + qo, ID_S, kk > 0 ? 1u : 0u);
+          mma_ss_w(tmem + 128 * sl + 64, vd + ko, dd + qo, ID_S, kk > 0 ? 1u : 0u);
+        }
+        mma_commit_w(BAR(C::B_SFULL + sl));
+        if (ul == tl.nU - 1) mma_commit_w(BAR(C::B_KVEMPTY + kb));  // K / V of this tile: last reader issued
+        if (u > 0 && !issue_kv(u - 1, pit, pfirst, pit != i)) { ok = false; break; }
+        pit = i;
+        pfirst = ul == 0;
+      }
+    }
+    if (ok && u > 0) ok = issue_kv(u - 1, pit, pfirst, true);
+    if (!ok) {
+      mma_commit_w(BAR(C::B_DRAIN));
+      mbar_wait_bounded(BAR(C::B_DRAIN), 0);
+    }
+    __syncwarp();
+  } else if (warp < 10) {
+    // ---------------- softmax: P^T, dS^T ----------------
+    const int w = (warp - 2) >> 2;           // units with (u & 1) == w
+    const int r = ((warp & 3) << 5) | lane;  // key row = TMEM lane
+    const uint32_t scol = tmem + (static_cast<uint32_t>(r & ~31) << 16) + 128 * w;
+    const float sl2 = p.scale_log2;
+    bool ok = true;
+    int u = 0;
+    for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x) {
+      const KeyLocalTile tl(t, p.n_ktiles, Hkv, S, W, groups);
+      const int kj = tl.k0 + r;
+      // queries that see this key row: [qa, qb)
+      const int qa = kj, qb = kj < S ? min(kj + W, S) : kj;
+      for (int ul = 0; ul < tl.nU; ++ul) {
+        const int uu = u++;
+        if ((uu & 1) != w) continue;
+        const int st = uu % C::NSQ;
+        int h, q0;
+        tl.unit(ul, groups, h, q0);
+        // SFULL first: it implies this unit's Q/dO stage load has completed,
+        // and the stage cannot be refilled before this unit's dV/dK products,
+        // so the QFULL parity test refers to exactly this load.  Waiting on
+        // QFULL makes the TMA writes of lse / delta visible to this thread.
+        if (!mbar_wait(BAR(C::B_SFULL + w), (uu >> 1) & 1, ab) ||
+            !mbar_wait(BAR(C::B_QFULL + st), (uu / C::NSQ) & 1, ab)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int lo = qa - q0, hi = qb - q0;
+        const float* sm_lse = reinterpret_cast<const float*>(smem + C::OFF_LSE + st * 2 * kUnit * 4);
+        const float* sm_di = sm_lse + kUnit;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          float s[32], dp[32];
+          tmem_ld32(scol + 32 * c, s);
+          tmem_ld32(scol + 64 + 32 * c, dp);
+          tmem_ld_wait();
+          const int a = min(max(lo - 32 * c, 0), 32), z = min(max(hi - 32 * c, 0), 32);
+          const uint32_t mz = z >= 32 ? 0xffffffffu : ((1u << z) - 1u);
+          const uint32_t ma = a >= 32 ? 0xffffffffu : ((1u << a) - 1u);
+          const uint32_t m = mz & ~ma;
+          uint32_t ppk[16], dpk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const int col = 32 * c + e;
+            const float p0 = (m & (1u << e)) ? ex2(fmaf(s[e], sl2, -sm_lse[col])) : 0.f;
+            const float p1 = (m & (2u << e)) ? ex2(fmaf(s[e + 1], sl2, -sm_lse[col + 1])) : 0.f;
+            ppk[e / 2] = E::pack(p0, p1);
+            dpk[e / 2] = E::pack(p0 * (dp[e] - sm_di[col]), p1 * (dp[e + 1] - sm_di[col + 1]));
+          }
+          // chunk c of P^T / dS^T overwrites score columns [16c, 16c+16) of
+          // S^T / dP^T, already consumed (columns [0, 32c+32) have been read)
+          tmem_st16(scol + 16 * c, ppk);
+          tmem_st16(scol + 64 + 16 * c, dpk);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(BAR(C::B_PFULL + w));
+      }
+    }
+  } else {
+    // ---------------- epilogue: dK, dV (+ dG fold-in) -> global ----------------
+    const int r = ((warp & 3) << 5) | lane;
+    const uint32_t lane_off = static_cast<uint32_t>(r & ~31) << 16;
+    for (int t = blockIdx.x, i = 0; t < n_tiles; t += gridDim.x, ++i) {
+      const KeyLocalTile tl(t, p.n_ktiles, Hkv, S, W, groups);
+      if (!mbar_wait(BAR(C::B_ACCFULL), i & 1, ab)) break;
+      tc_fence_after();
+      const int kj = tl.k0 + r;
+      const bool row_ok = kj < S;
+      // global-row gradients that belong to this key position
+      const int blk = kj / W;
+      const int64_t gbase = (static_cast<int64_t>(tl.b) * Hkv + tl.hk) * static_cast<int64_t>(p.NG);
+      int grow[5];
+      float gsc[5];
+      int ng = 0;
+      if (row_ok) {
+        if (kj == blk * W) {
+          grow[ng] = blk * R;
+          gsc[ng] = 1.f;
+          ++ng;
+        }
+        if (R > 1) {
+          float rs = 1.f;
+          if (p.relay_scale) rs = E::to_f(E::from_f(expf(p.relay_scale[tl.hk])));
+          const int32_t* src = p.gsrc + ((static_cast<int64_t>(tl.b) * Hkv + tl.hk) * p.NB + blk) * p.top_k;
+          for (int q = 0; q < p.top_k; ++q)
+            if (src[q] == kj) {
+              grow[ng] = blk * R + 1 + q;
+              gsc[ng] = rs;
+              ++ng;
+            }
+        }
+      }
+#pragma unroll 1
+      for (int which = 0; which < 2; ++which) {  // 0: dK (scaled), 1: dV
+        const uint32_t acc = tmem + lane_off + (which == 0 ? C::COL_DK : C::COL_DV);
+        const float mul = which == 0 ? p.scale : 1.f;
+        const float* dg = which == 0 ? p.dgk : p.dgv;
+        T* drow = which == 0
+                      ? reinterpret_cast<T*>(p.dk) + tl.b * p.dk_sb + tl.hk * p.dk_sh + static_cast<int64_t>(kj) * p.dk_ss
+                      : reinterpret_cast<T*>(p.dv) + tl.b * p.dv_sb + tl.hk * p.dv_sh + static_cast<int64_t>(kj) * p.dv_ss;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          float v[32];
+          tmem_ld32(acc + 32 * c, v);
+          tmem_ld_wait();
+          if (which == 1 && c == D / 32 - 1) {  // every TMEM read of this tile's dK / dV done
+            tc_fence_before();
+            mbar_arrive(BAR(C::B_ACCFREE));
+          }
+          if (row_ok) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] *= mul;
+            for (int gi = 0; gi < ng; ++gi) {
+              const float* gr = dg + (gbase + grow[gi]) * D + 32 * c;
+#pragma unroll
+              for (int e = 0; e < 32; e += 4) {
+                const float4 a4 = *reinterpret_cast<const float4*>(gr + e);
+                v[e] += gsc[gi] * a4.x;
+                v[e + 1] += gsc[gi] * a4.y;
+                v[e + 2] += gsc[gi] * a4.z;
+                v[e + 3] += gsc[gi] * a4.w;
+              }
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 a4;
+              a4.x = E::pack(v[8 * q + 0], v[8 * q + 1]);
+              a4.y = E::pack(v[8 * q + 2], v[8 * q + 3]);
+              a4.z = E::pack(v[8 * q + 4], v[8 * q + 5]);
+              a4.w = E::pack(v[8 * q + 6], v[8 * q + 7]);
+              *reinterpret_cast<uint4*>(drow + 32 * c + 8 * q) = a4;
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+// ===========================================================================
 // dG = sum over splits of the partials (fixed order).
 // ===========================================================================
 __global__ void __launch_bounds__(256) reduce_kernel(const float4* __restrict__ pk, const float4* __restrict__ pv,
@@ -912,9 +1251,11 @@ static cudaError_t launch_bwd_t(const BwdLaunch& L, cudaStream_t st) {
   }
   const KeyPassParams& lp = L.local;
   {
-    auto kern = keypass_kernel<D, BF16, false>;
-    if ((e = set_smem(kern, KeyCfg<D>::SMEM)) != cudaSuccess) return e;
-    kern<<<dim3(lp.n_ktiles, Hkv, B), 320, KeyCfg<D>::SMEM, st>>>(lp);
+    auto kern = keylocal_kernel<D, BF16>;
+    if ((e = set_smem(kern, KeyLocalCfg<D>::SMEM)) != cudaSuccess) return e;
+    const int n_tiles = lp.n_ktiles * Hkv * B;
+    kern<<<dim3(n_tiles < sm_count() ? n_tiles : sm_count()), KeyLocalCfg<D>::THREADS, KeyLocalCfg<D>::SMEM, st>>>(
+        lp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   {
