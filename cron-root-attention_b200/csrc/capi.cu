@@ -143,7 +143,7 @@ int global_splits(int batch, int kv_heads, int seq_len, int NG) {
   const int n_gtiles = (NG + kTile - 1) / kTile;
   const int n_qtiles = (seq_len + kTile - 1) / kTile;
   const long long base = static_cast<long long>(batch) * kv_heads * n_gtiles;
-  long long s = (296 + base - 1) / base;
+  long long s = (888 + base - 1) / base;
   if (s > 32) s = 32;
   if (s > n_qtiles) s = n_qtiles;
   if (s < 1) s = 1;
