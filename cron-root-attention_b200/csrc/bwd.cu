@@ -9,22 +9,24 @@
 //
 // Kernels, in launch order:
 //   delta_kernel     Di and lse*log2(e), padded to whole 128-query tiles.
-//   keypass<GLOBAL>  one CTA per (128 global rows, query split): dG_k / dG_v
+//   keyglobal_kernel one CTA per (128 global rows, query split): dG_k / dG_v
 //                    over every query that sees the rows; fp32 partials per
 //                    split (no atomics).
 //   reduce_kernel    sums the splits in a fixed order -> dG (fp32).
 //   dalpha_kernel    d(relay_log_scale) = sum over relay rows of dG * G
 //                    (only when a relay scale is used).
-//   keypass<LOCAL>   one CTA per 128-key tile: dK / dV over the local band,
-//                    then folds in dG of the tile's strided key and of every
-//                    relay row whose source lies in the tile, and stores.
+//   keylocal_kernel  persistent (one CTA per SM) over 128-key tiles: dK / dV
+//                    over the local band, then folds in dG of the tile's
+//                    strided key and of every relay row whose source lies in
+//                    the tile, and stores.
 //   dq_kernel        persistent (one CTA per SM) over 128-query tiles: dQ over
 //                    band + global prefix.
 // The result is deterministic: every sum has a fixed order.
 //
 // The attention kernels use the warp roles of the forward (fwd.cu): warp 0
-// TMA producer, warp 1 single-thread tcgen05 issuer + TMEM owner, warps 2-5
-// and 6-9 two softmax warpgroups, one row per thread (TMEM lane = row).
+// TMA producer, warp 1 tcgen05 issuer (whole warp, one elected lane) + TMEM
+// owner, warps 2-5 and 6-9 two softmax warpgroups, one row per thread (TMEM
+// lane = row); the persistent kernels add an epilogue warpgroup.
 #include "geom.cuh"
 #include "params.h"
 #include "sm100.cuh"
@@ -468,9 +470,10 @@ extern "C" __attribute__((visibility("default"))) int cra_dq_prof(unsigned long 
 #endif
 
 // ===========================================================================
-// Key-centric pass.  Thread r owns key row r of the CTA's 128-row key tile
-// (K/V rows in LOCAL mode, global rows G in GLOBAL mode).  The queries that
-// see the tile are walked in 64-query units; per unit:
+// Key-centric pass over the global rows G (strided + relay keys).  Thread r
+// owns global row r of the CTA's 128-row tile.  The queries that see the
+// tile (a contiguous range starting at first_query_seeing) are split into
+// n_split ranges, one per CTA, walked in 64-query units; per unit:
 //   S^T = K Q_u^T, dP^T = V dO_u^T  (one of two TMEM slots),
 //   P^T, dS^T (16-bit) written back into the same TMEM slot,
 //   dV += P^T dO_u,  dK += dS^T Q_u  (TMEM accumulators; A operands read
@@ -502,8 +505,8 @@ struct KeyCfg {
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
-template <int D, bool BF16, bool GLOBAL>
-__global__ void __launch_bounds__(320, 1) keypass_kernel(const __grid_constant__ KeyPassParams p) {
+template <int D, bool BF16>
+__global__ void __launch_bounds__(320, 1) keyglobal_kernel(const __grid_constant__ KeyPassParams p) {
   using C = KeyCfg<D>;
   using E = Elt<BF16>;
   using T = typename E::T;
@@ -516,22 +519,14 @@ __global__ void __launch_bounds__(320, 1) keypass_kernel(const __grid_constant__
   const int Spad = ((S + kTile - 1) / kTile) * kTile;
   const int groups = p.kv_groups;
 
-  // key tile and the 64-query units [t_lo, t_hi) it meets (per group head)
-  int k0, split = 0, t_lo, t_hi;
-  if (GLOBAL) {
-    const int gt = static_cast<int>(blockIdx.x) / p.n_split;
-    split = static_cast<int>(blockIdx.x) % p.n_split;
-    k0 = gt * kTile;
-    const int tmin = first_query_seeing(k0, S, W, R) / kUnit;
-    const int tot = n_units - tmin;
-    t_lo = tmin + static_cast<int>((static_cast<int64_t>(tot) * split) / p.n_split);
-    t_hi = tmin + static_cast<int>((static_cast<int64_t>(tot) * (split + 1)) / p.n_split);
-  } else {
-    k0 = (p.n_ktiles - 1 - static_cast<int>(blockIdx.x)) * kTile;
-    const int qlast = min(k0 + kTile - 1 + W - 1, S - 1);
-    t_lo = k0 / kUnit;
-    t_hi = qlast / kUnit + 1;
-  }
+  // global-row tile and this split's 64-query units [t_lo, t_hi) (per group head)
+  const int gt = static_cast<int>(blockIdx.x) / p.n_split;
+  const int split = static_cast<int>(blockIdx.x) % p.n_split;
+  const int k0 = gt * kTile;
+  const int tmin = first_query_seeing(k0, S, W, R) / kUnit;
+  const int tot = n_units - tmin;
+  const int t_lo = tmin + static_cast<int>((static_cast<int64_t>(tot) * split) / p.n_split);
+  const int t_hi = tmin + static_cast<int>((static_cast<int64_t>(tot) * (split + 1)) / p.n_split);
   const int nT = t_hi - t_lo;
   const int nU = nT * groups;
 
@@ -652,18 +647,11 @@ __global__ void __launch_bounds__(320, 1) keypass_kernel(const __grid_constant__
   } else {
     const int w = (warp - 2) >> 2;           // softmax warpgroup: units with (u & 1) == w
     const int r = ((warp & 3) << 5) | lane;  // key row = TMEM lane
-    const int kj = k0 + r;                   // key position (LOCAL) or global row (GLOBAL)
+    const int kj = k0 + r;                   // global row
     const uint32_t lane_off = static_cast<uint32_t>(r & ~31) << 16;
     const float sl2 = p.scale_log2;
-    // queries that see this key row: [qa, qb)
-    int qa, qb;
-    if (GLOBAL) {
-      qa = kj < p.NG ? first_query_seeing(kj, S, W, R) : S;
-      qb = S;
-    } else {
-      qa = kj;
-      qb = kj < S ? min(kj + W, S) : kj;
-    }
+    // queries that see this global row: [qa, S)
+    const int qa = kj < p.NG ? first_query_seeing(kj, S, W, R) : S, qb = S;
     const uint32_t scol = tmem + lane_off + 128 * w;
     bool ok = true;
     for (int u = w; u < nU; u += 2) {
@@ -710,92 +698,31 @@ __global__ void __launch_bounds__(320, 1) keypass_kernel(const __grid_constant__
       mbar_arrive(BAR(C::B_PFULL + w));
     }
     // ------------------------------------------------------------ epilogue
-    // warpgroup 0 writes dK, warpgroup 1 writes dV
+    // warpgroup 0 writes dG_k partials, warpgroup 1 dG_v partials
     const bool have = nU > 0;
     if (ok && (!have || mbar_wait(BAR(C::B_DONE), 0, ab))) {
       tc_fence_after();
       const uint32_t acc = tmem + lane_off + (w == 0 ? C::COL_DK : C::COL_DV);
       const float mul = w == 0 ? p.scale : 1.f;
-      if (GLOBAL) {
-        const bool row_ok = kj < p.NG;
-        float* dst = (w == 0 ? p.part_k : p.part_v) +
-                     ((static_cast<int64_t>(split) * p.B + b) * gridDim.y + hk) * static_cast<int64_t>(p.NG) * D +
-                     static_cast<int64_t>(kj) * D;
+      const bool row_ok = kj < p.NG;
+      float* dst = (w == 0 ? p.part_k : p.part_v) +
+                   ((static_cast<int64_t>(split) * p.B + b) * gridDim.y + hk) * static_cast<int64_t>(p.NG) * D +
+                   static_cast<int64_t>(kj) * D;
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          float v[32];
-          if (have) {
-            tmem_ld32(acc + 32 * c, v);
-            tmem_ld_wait();
-          } else {
-#pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] = 0.f;
-          }
-          if (row_ok) {
-#pragma unroll
-            for (int e = 0; e < 32; e += 4)
-              *reinterpret_cast<float4*>(dst + 32 * c + e) =
-                  make_float4(v[e] * mul, v[e + 1] * mul, v[e + 2] * mul, v[e + 3] * mul);
-          }
-        }
-      } else {
-        const bool row_ok = kj < S;
-        // global-row gradients that belong to this key position
-        const int blk = kj / W;
-        const int64_t gbase = (static_cast<int64_t>(b) * gridDim.y + hk) * static_cast<int64_t>(p.NG);
-        const float* dg = w == 0 ? p.dgk : p.dgv;
-        int grow[5];
-        float gsc[5];
-        int ng = 0;
-        if (row_ok) {
-          if (kj == blk * W) {
-            grow[ng] = blk * R;
-            gsc[ng] = 1.f;
-            ++ng;
-          }
-          if (R > 1) {
-            float rs = 1.f;
-            if (p.relay_scale) rs = E::to_f(E::from_f(expf(p.relay_scale[hk])));
-            const int32_t* src = p.gsrc + ((static_cast<int64_t>(b) * gridDim.y + hk) * p.NB + blk) * p.top_k;
-            for (int t = 0; t < p.top_k; ++t)
-              if (src[t] == kj) {
-                grow[ng] = blk * R + 1 + t;
-                gsc[ng] = rs;
-                ++ng;
-              }
-          }
-        }
-        T* drow = w == 0 ? reinterpret_cast<T*>(p.dk) + b * p.dk_sb + hk * p.dk_sh + static_cast<int64_t>(kj) * p.dk_ss
-                         : reinterpret_cast<T*>(p.dv) + b * p.dv_sb + hk * p.dv_sh + static_cast<int64_t>(kj) * p.dv_ss;
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          float v[32];
+      for (int c = 0; c < D / 32; ++c) {
+        float v[32];
+        if (have) {
           tmem_ld32(acc + 32 * c, v);
           tmem_ld_wait();
-          if (row_ok) {
+        } else {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] *= mul;
-            for (int gi = 0; gi < ng; ++gi) {
-              const float* gr = dg + (gbase + grow[gi]) * D + 32 * c;
+          for (int e = 0; e < 32; ++e) v[e] = 0.f;
+        }
+        if (row_ok) {
 #pragma unroll
-              for (int e = 0; e < 32; e += 4) {
-                const float4 a = *reinterpret_cast<const float4*>(gr + e);
-                v[e] += gsc[gi] * a.x;
-                v[e + 1] += gsc[gi] * a.y;
-                v[e + 2] += gsc[gi] * a.z;
-                v[e + 3] += gsc[gi] * a.w;
-              }
-            }
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint4 a;
-              a.x = E::pack(v[8 * q + 0], v[8 * q + 1]);
-              a.y = E::pack(v[8 * q + 2], v[8 * q + 3]);
-              a.z = E::pack(v[8 * q + 4], v[8 * q + 5]);
-              a.w = E::pack(v[8 * q + 6], v[8 * q + 7]);
-              *reinterpret_cast<uint4*>(drow + 32 * c + 8 * q) = a;
-            }
-          }
+          for (int e = 0; e < 32; e += 4)
+            *reinterpret_cast<float4*>(dst + 32 * c + e) =
+                make_float4(v[e] * mul, v[e + 1] * mul, v[e + 2] * mul, v[e + 3] * mul);
         }
       }
     }
@@ -809,7 +736,8 @@ __global__ void __launch_bounds__(320, 1) keypass_kernel(const __grid_constant__
 // ===========================================================================
 // Local key pass, persistent.  One CTA per SM walks the local key tiles t =
 // blockIdx.x, blockIdx.x + gridDim.x, ... (kt fastest, latest keys first).
-// Per tile the work is the key-centric pass above in LOCAL mode; across tiles
+// Per tile the work is the key-centric pass above, over K / V rows of the
+// local band instead of global rows; across tiles
 //   * K / V are double-buffered (tile i in buffer i & 1), so the next tile's
 //     K / V arrive while the current tile runs;
 //   * the Q / dO unit stream, the MMA issue and the two softmax warpgroups
@@ -1232,7 +1160,7 @@ static cudaError_t launch_bwd_t(const BwdLaunch& L, cudaStream_t st) {
   const int Hkv = gp.H / gp.kv_groups;
   const int n_gtiles = (gp.NG + kTile - 1) / kTile;
   {
-    auto kern = keypass_kernel<D, BF16, true>;
+    auto kern = keyglobal_kernel<D, BF16>;
     if ((e = set_smem(kern, KeyCfg<D>::SMEM)) != cudaSuccess) return e;
     kern<<<dim3(n_gtiles * gp.n_split, Hkv, B), 320, KeyCfg<D>::SMEM, st>>>(gp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
