@@ -247,19 +247,51 @@ def run_ours(args, rank, world, local_rank):
                                                None, gk.data_ptr(), gv.data_ptr(), gsrc.data_ptr(), sp),
                      args.steps)
 
-    # --- end to end through the public API with host buffers: H2D of q, k, v,
-    # dO from pinned memory, fwd + bwd, D2H of dq, dk, dv into pinned memory
-    out_host = [torch.empty_like(host[0]).pin_memory() for _ in range(3)]
+    # --- end to end through the public API with host buffers: every step copies
+    # q, k, v, dO from pinned memory to the device, runs fwd + bwd, and copies
+    # dq, dk, dv back into pinned memory.  The copies are pipelined the way a
+    # serving loop would: step i + 1's inputs go up (H2D stream) and step
+    # i - 1's gradients come down (D2H stream) while step i computes; PCIe is
+    # full duplex.  Device inputs and host outputs are double-buffered; events
+    # order each buffer's reuse.
+    h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    dev_in = [[torch.empty_like(t) for t in (q, k, v, do)] for _ in range(2)]
+    out_host = [[torch.empty_like(host[0]).pin_memory() for _ in range(3)] for _ in range(2)]
+    in_free = [None, None]    # event: compute finished reading dev_in[s]
+    out_free = [None, None]   # event: D2H finished writing out_host[s]
 
-    def e2e_step():
-        qd, kd, vd, dod = (h.to(dev, non_blocking=True) for h in host)
-        _, grads = step(qd, kd, vd, dod)
-        for hbuf, g in zip(out_host, grads):
-            hbuf.copy_(g, non_blocking=True)
+    def e2e_run(n):
+        h2d.wait_stream(stream)  # the first upload starts inside the timed region
+        for i in range(n):
+            s = i & 1
+            with torch.cuda.stream(h2d):
+                if in_free[s] is not None:
+                    h2d.wait_event(in_free[s])
+                for dst, src in zip(dev_in[s], host):
+                    dst.copy_(src, non_blocking=True)
+                up = torch.cuda.Event()
+                up.record(h2d)
+            stream.wait_event(up)
+            _, grads = step(*(t.detach() for t in dev_in[s]))
+            done = torch.cuda.Event()
+            done.record(stream)
+            in_free[s] = done
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(done)
+                if out_free[s] is not None:
+                    d2h.wait_event(out_free[s])
+                for hbuf, g in zip(out_host[s], grads):
+                    g.record_stream(d2h)
+                    hbuf.copy_(g, non_blocking=True)
+                down = torch.cuda.Event()
+                down.record(d2h)
+                out_free[s] = down
+        stream.wait_stream(h2d)
+        stream.wait_stream(d2h)
 
-    for _ in range(2):
-        e2e_step()
-    ms_e2e = timed(e2e_step, max(1, min(args.steps, 5)))
+    e2e_run(2)
+    n_e2e = max(2, min(args.steps, 8))
+    ms_e2e = timed(lambda: e2e_run(n_e2e), 1) / n_e2e
     nbytes = host[0].numel() * host[0].element_size()
 
     assert cra.check_device_errors(dev) == 0, "a kernel gave up on a bounded wait"
@@ -299,7 +331,8 @@ def run_ours(args, rank, world, local_rank):
                      "relay_build_ms": ms_relay,
                      "relay_build_gbs": (2 * B * H * S * D * 2 + 2 * B * H * NG * D * 2) / (ms_relay * 1e-3) / 1e9},
         "e2e": {"value": world * (f_fwd + f_bwd) / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
-                "ms_per_step": ms_e2e, "h2d_bytes_per_step": 4 * nbytes, "d2h_bytes_per_step": 3 * nbytes},
+                "ms_per_step": ms_e2e, "h2d_bytes_per_step": 4 * nbytes, "d2h_bytes_per_step": 3 * nbytes,
+                "steps": n_e2e, "copies": "pipelined across steps on separate H2D / D2H streams"},
         "gpu_launches": 7 * args.steps,
         "clocks": clocks,
     }
