@@ -97,13 +97,15 @@ __global__ void __launch_bounds__(256) delta_kernel(const void* __restrict__ op,
 // Counters live in registers and are flushed once per warp at exit.
 #ifdef CRA_PROF
 __device__ unsigned long long g_dq_prof[32];
+__device__ unsigned long long g_kl_prof[32];
+#define PROF_ARR g_dq_prof
 #define PROF_DECL unsigned long long pacc[32] = {};
 #define PROF_T(v) const unsigned long long v = clock64()
 #define PROF_ADD(k, t0) (pacc[k] += clock64() - (t0))
 #define PROF_CNT(k, n) (pacc[k] += static_cast<unsigned long long>(n))
 #define PROF_FLUSH()                                                     \
   if ((threadIdx.x & 31) == 0)                                           \
-    _Pragma("unroll") for (int k = 0; k < 32; ++k) if (pacc[k]) atomicAdd(&g_dq_prof[k], pacc[k]);
+    _Pragma("unroll") for (int k = 0; k < 32; ++k) if (pacc[k]) atomicAdd(&PROF_ARR[k], pacc[k]);
 #else
 #define PROF_DECL
 #define PROF_T(v)
@@ -467,6 +469,14 @@ extern "C" __attribute__((visibility("default"))) int cra_dq_prof(unsigned long 
   }
   return 0;
 }
+extern "C" __attribute__((visibility("default"))) int cra_kl_prof(unsigned long long* out32, int reset) {
+  cudaMemcpyFromSymbol(out32, g_kl_prof, sizeof(g_kl_prof));
+  if (reset) {
+    unsigned long long z[32] = {};
+    cudaMemcpyToSymbol(g_kl_prof, z, sizeof(z));
+  }
+  return 0;
+}
 #endif
 
 // ===========================================================================
@@ -785,6 +795,11 @@ struct KeyLocalTile {
   }
 };
 
+#ifdef CRA_PROF
+#undef PROF_ARR
+#define PROF_ARR g_kl_prof
+#endif
+
 template <int D, bool BF16>
 __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant__ KeyPassParams p) {
   using C = KeyLocalCfg<D>;
@@ -804,6 +819,7 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
   const Abort ab{abort_flag, p.err};
+  PROF_DECL
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2; ++s) {
@@ -836,7 +852,9 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
       for (int t = blockIdx.x, i = 0; ok && t < n_tiles; t += gridDim.x, ++i) {
         const KeyLocalTile tl(t, p.n_ktiles, Hkv, S, W, groups);
         const int kb = i & 1;
+        PROF_T(tk);
         if (i >= 2 && !mbar_wait(BAR(C::B_KVEMPTY + kb), ((i >> 1) - 1) & 1, ab)) break;
+        PROF_ADD(0, tk);
         mbar_expect_tx(BAR(C::B_KVFULL + kb), 2 * C::TB);
         const uint32_t kd = sbase + C::OFF_KV + 2 * kb * C::TB;
         for (int c = 0; c < D / 64; ++c) {
@@ -846,7 +864,9 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
         ++nkv;
         for (int ul = 0; ul < tl.nU; ++ul, ++e) {
           const int st = e % C::NSQ;
+          PROF_T(tq);
           if (e >= C::NSQ && !mbar_wait(BAR(C::B_QEMPTY + st), ((e / C::NSQ) - 1) & 1, ab)) { ok = false; break; }
+          PROF_ADD(1, tq);
           int h, q0;
           tl.unit(ul, groups, h, q0);
           const uint32_t qd = sbase + C::OFF_Q + st * 2 * C::UB;
@@ -876,8 +896,12 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
     // dV += P^T dO, dK += dS^T Q for unit i (of tile iteration iti)
     auto issue_kv = [&](int i, int iti, bool first, bool last) -> bool {
       const int st = i % C::NSQ, sl = i & 1;
+      PROF_T(tp);
       if (!warp_wait(BAR(C::B_PFULL + sl), (i >> 1) & 1, ab)) return false;
+      PROF_ADD(4, tp);
+      PROF_T(ta);
       if (first && iti >= 1 && !warp_wait(BAR(C::B_ACCFREE), (iti - 1) & 1, ab)) return false;
+      PROF_ADD(5, ta);
       tc_fence_after();
       const uint32_t qd = sbase + C::OFF_Q + st * 2 * C::UB;
       const uint64_t dod = sdesc(qd + C::UB, kUnit * 128, 1024), qdd = sdesc(qd, kUnit * 128, 1024);
@@ -891,19 +915,24 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
       if (last) mma_commit_w(BAR(C::B_ACCFULL));
       return true;
     };
+    PROF_T(tstart);
     int u = 0, pit = -1;
     bool pfirst = false;
     for (int t = blockIdx.x, i = 0; ok && t < n_tiles; t += gridDim.x, ++i) {
       const KeyLocalTile tl(t, p.n_ktiles, Hkv, S, W, groups);
       const int kb = i & 1;
+      PROF_T(tk);
       if (!warp_wait(BAR(C::B_KVFULL + kb), (i >> 1) & 1, ab)) { ok = false; break; }
+      PROF_ADD(6, tk);
       const uint64_t kd = sdesc(sbase + C::OFF_KV + 2 * kb * C::TB, 16, 1024);
       const uint64_t vd = sdesc(sbase + C::OFF_KV + (2 * kb + 1) * C::TB, 16, 1024);
       for (int ul = 0; ul < tl.nU; ++ul, ++u) {
         const int st = u % C::NSQ, sl = u & 1;
         // slot sl was last read by the dV / dK products of unit u - 2, issued
         // before this S^T / dP^T (in-order execution)
+        PROF_T(tq);
         if (!warp_wait(BAR(C::B_QFULL + st), (u / C::NSQ) & 1, ab)) { ok = false; break; }
+        PROF_ADD(7, tq);
         tc_fence_after();
         const uint32_t qa = sbase + C::OFF_Q + st * 2 * C::UB;
         const uint64_t qd = sdesc(qa, 16, 1024), dd = sdesc(qa + C::UB, 16, 1024);
@@ -922,6 +951,9 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
       }
     }
     if (ok && u > 0) ok = issue_kv(u - 1, pit, pfirst, true);
+    PROF_ADD(9, tstart);
+    PROF_CNT(30, u);
+    PROF_CNT(31, 1);
     if (!ok) {
       mma_commit_w(BAR(C::B_DRAIN));
       mbar_wait_bounded(BAR(C::B_DRAIN), 0);
@@ -950,11 +982,14 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
         // and the stage cannot be refilled before this unit's dV/dK products,
         // so the QFULL parity test refers to exactly this load.  Waiting on
         // QFULL makes the TMA writes of lse / delta visible to this thread.
+        PROF_T(ts);
         if (!mbar_wait(BAR(C::B_SFULL + w), (uu >> 1) & 1, ab) ||
             !mbar_wait(BAR(C::B_QFULL + st), (uu / C::NSQ) & 1, ab)) {
           ok = false;
           break;
         }
+        PROF_ADD(12, ts);
+        PROF_T(tb);
         tc_fence_after();
         const int lo = qa - q0, hi = qb - q0;
         const float* sm_lse = reinterpret_cast<const float*>(smem + C::OFF_LSE + st * 2 * kUnit * 4);
@@ -986,6 +1021,7 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(BAR(C::B_PFULL + w));
+        PROF_ADD(13, tb);
       }
     }
   } else {
@@ -994,7 +1030,10 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
     const uint32_t lane_off = static_cast<uint32_t>(r & ~31) << 16;
     for (int t = blockIdx.x, i = 0; t < n_tiles; t += gridDim.x, ++i) {
       const KeyLocalTile tl(t, p.n_ktiles, Hkv, S, W, groups);
+      PROF_T(te);
       if (!mbar_wait(BAR(C::B_ACCFULL), i & 1, ab)) break;
+      PROF_ADD(16, te);
+      PROF_T(tb);
       tc_fence_after();
       const int kj = tl.k0 + r;
       const bool row_ok = kj < S;
@@ -1065,8 +1104,10 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
           }
         }
       }
+      PROF_ADD(17, tb);
     }
   }
+  PROF_FLUSH()
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
