@@ -1069,37 +1069,44 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
         T* drow = which == 0
                       ? reinterpret_cast<T*>(p.dk) + tl.b * p.dk_sb + tl.hk * p.dk_sh + static_cast<int64_t>(kj) * p.dk_ss
                       : reinterpret_cast<T*>(p.dv) + tl.b * p.dv_sb + tl.hk * p.dv_sh + static_cast<int64_t>(kj) * p.dv_ss;
+        // two 32-column TMEM loads per wait: half the round trips before the
+        // accumulators can be released
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          float v[32];
-          tmem_ld32(acc + 32 * c, v);
+        for (int c2 = 0; c2 < D / 64; ++c2) {
+          float v[2][32];
+          tmem_ld32(acc + 64 * c2, v[0]);
+          tmem_ld32(acc + 64 * c2 + 32, v[1]);
           tmem_ld_wait();
-          if (which == 1 && c == D / 32 - 1) {  // every TMEM read of this tile's dK / dV done
+          if (which == 1 && c2 == D / 64 - 1) {  // every TMEM read of this tile's dK / dV done
             tc_fence_before();
             mbar_arrive(BAR(C::B_ACCFREE));
           }
           if (row_ok) {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] *= mul;
-            for (int gi = 0; gi < ng; ++gi) {
-              const float* gr = dg + (gbase + grow[gi]) * D + 32 * c;
+            for (int h2 = 0; h2 < 2; ++h2) {
+              const int c = 2 * c2 + h2;
 #pragma unroll
-              for (int e = 0; e < 32; e += 4) {
-                const float4 a4 = *reinterpret_cast<const float4*>(gr + e);
-                v[e] += gsc[gi] * a4.x;
-                v[e + 1] += gsc[gi] * a4.y;
-                v[e + 2] += gsc[gi] * a4.z;
-                v[e + 3] += gsc[gi] * a4.w;
+              for (int e = 0; e < 32; ++e) v[h2][e] *= mul;
+              for (int gi = 0; gi < ng; ++gi) {
+                const float* gr = dg + (gbase + grow[gi]) * D + 32 * c;
+#pragma unroll
+                for (int e = 0; e < 32; e += 4) {
+                  const float4 a4 = *reinterpret_cast<const float4*>(gr + e);
+                  v[h2][e] += gsc[gi] * a4.x;
+                  v[h2][e + 1] += gsc[gi] * a4.y;
+                  v[h2][e + 2] += gsc[gi] * a4.z;
+                  v[h2][e + 3] += gsc[gi] * a4.w;
+                }
               }
-            }
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint4 a4;
-              a4.x = E::pack(v[8 * q + 0], v[8 * q + 1]);
-              a4.y = E::pack(v[8 * q + 2], v[8 * q + 3]);
-              a4.z = E::pack(v[8 * q + 4], v[8 * q + 5]);
-              a4.w = E::pack(v[8 * q + 6], v[8 * q + 7]);
-              *reinterpret_cast<uint4*>(drow + 32 * c + 8 * q) = a4;
+              for (int q = 0; q < 4; ++q) {
+                uint4 a4;
+                a4.x = E::pack(v[h2][8 * q + 0], v[h2][8 * q + 1]);
+                a4.y = E::pack(v[h2][8 * q + 2], v[h2][8 * q + 3]);
+                a4.z = E::pack(v[h2][8 * q + 4], v[h2][8 * q + 5]);
+                a4.w = E::pack(v[h2][8 * q + 6], v[h2][8 * q + 7]);
+                *reinterpret_cast<uint4*>(drow + 32 * c + 8 * q) = a4;
+              }
             }
           }
         }
