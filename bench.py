@@ -329,7 +329,8 @@ def run_ours(args, rank, world, local_rank):
                      "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
                      "peak_source": f"{peak_src} bf16 dense (burst)", "kernel_ms": ms_kernel,
                      "relay_build_ms": ms_relay,
-                     "relay_build_gbs": (2 * B * H * S * D * 2 + 2 * B * H * NG * D * 2) / (ms_relay * 1e-3) / 1e9},
+                     # K read once (norms) + the chosen K / V rows read and written as G
+                     "relay_build_gbs": (B * H * S * D * 2 + 4 * B * H * NG * D * 2) / (ms_relay * 1e-3) / 1e9},
         "e2e": {"value": world * (f_fwd + f_bwd) / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
                 "ms_per_step": ms_e2e, "h2d_bytes_per_step": 4 * nbytes, "d2h_bytes_per_step": 3 * nbytes,
                 "steps": n_e2e, "copies": "pipelined across steps on separate H2D / D2H streams"},

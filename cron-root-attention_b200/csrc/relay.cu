@@ -20,9 +20,11 @@
 // core.py:1042-1087) so that the attention kernels see one prefix-visible
 // list (geom.cuh).
 //
-// One warp per block; D/8 lanes cooperate on one row with 16-byte loads, so a
-// warp reads 32*16 = 512 contiguous bytes per step: the scan is a single
-// coalesced pass over K, bound by HBM bandwidth.
+// One 4-warp CTA per block: the warps take interleaved row steps (D/8 lanes
+// cooperate on one row with 16-byte loads, so a warp reads 32*16 = 512
+// contiguous bytes per step), then merge their top-4 lists through shared
+// memory.  The scan is a single coalesced pass over K; four warps per block
+// keep enough loads in flight for it to run at HBM bandwidth.
 #include "geom.cuh"
 #include "params.h"
 #include "sm100.cuh"
@@ -47,9 +49,8 @@ __global__ void __launch_bounds__(128) relay_build_kernel(const void* __restrict
   constexpr int LPR = D / 8;          // lanes per row
   constexpr int RPS = 32 / LPR;       // rows per warp step
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r = blockIdx.x * 4 + warp;
+  const int r = blockIdx.x;
   const int h = blockIdx.y, b = blockIdx.z;
-  if (r >= NB) return;
   const T* k = reinterpret_cast<const T*>(kp) + b * k_sb + h * k_sh;
   const T* v = reinterpret_cast<const T*>(vp) + b * v_sb + h * v_sh;
   const int row_lo = r * W;
@@ -61,7 +62,7 @@ __global__ void __launch_bounds__(128) relay_build_kernel(const void* __restrict
   for (int t = 0; t < 4; ++t) best[t] = Cand{-1.f, row_lo};
 
   if (R > 1) {
-    for (int i0 = row_lo; i0 < row_hi; i0 += RPS) {
+    for (int i0 = row_lo + warp * RPS; i0 < row_hi; i0 += 4 * RPS) {
       const int i = i0 + sub;
       float acc = 0.f;
       if (i < row_hi) {
@@ -112,6 +113,36 @@ __global__ void __launch_bounds__(128) relay_build_kernel(const void* __restrict
           }
         }
       }
+    }
+  }
+  // merge the four warps' lists (selection order is a total order: norm, then
+  // lower index, so merging in any order gives the same result)
+  __shared__ float s_n[4][4];
+  __shared__ int s_i[4][4];
+  if (R > 1 && lane == 0) {
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      s_n[warp][t] = best[t].n;
+      s_i[warp][t] = best[t].i;
+    }
+  }
+  __syncthreads();
+  if (warp != 0) return;
+  if (R > 1) {
+    if (lane == 0) {
+      for (int w2 = 1; w2 < 4; ++w2)
+#pragma unroll
+        for (int t2 = 0; t2 < 4; ++t2) {
+          Cand c{s_n[w2][t2], s_i[w2][t2]};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            if (better(c, best[t])) {
+              const Cand tmp = best[t];
+              best[t] = c;
+              c = tmp;
+            }
+          }
+        }
     }
     // broadcast lane 0's result
 #pragma unroll
@@ -165,7 +196,7 @@ cudaError_t launch_relay_build(int D, bool bf16, const void* k, const void* v, c
                                int B, int Hkv, int S, int W, int top_k, int R, int pos0, const float* log_scale,
                                void* gk, void* gv, int32_t* gsrc, cudaStream_t stream) {
   const int NB = (S + W - 1) / W;
-  dim3 grid((NB + 3) / 4, Hkv, B);
+  dim3 grid(NB, Hkv, B);
 #define CRA_RELAY(DD, BB)                                                                                          \
   relay_build_kernel<DD, BB><<<grid, 128, 0, stream>>>(k, v, ks[0], ks[1], ks[2], vs[0], vs[1], vs[2], Hkv, S, W, \
                                                        NB, top_k, R, pos0, log_scale, gk, gv, gsrc)
