@@ -20,11 +20,10 @@
 // core.py:1042-1087) so that the attention kernels see one prefix-visible
 // list (geom.cuh).
 //
-// One 4-warp CTA per block: the warps take interleaved row steps (D/8 lanes
-// cooperate on one row with 16-byte loads, so a warp reads 32*16 = 512
-// contiguous bytes per step), then merge their top-4 lists through shared
-// memory.  The scan is a single coalesced pass over K; four warps per block
-// keep enough loads in flight for it to run at HBM bandwidth.
+// One warp per block, one lane per row: a lane loads its whole row (D/8
+// 16-byte loads, all in flight before use), computes the fp32 norm and keeps
+// its own top-4; the warp merges the 32 lists with a shuffle tree.  The scan
+// is a single pass over K with 8 KB in flight per warp.
 #include "geom.cuh"
 #include "params.h"
 #include "sm100.cuh"
@@ -49,8 +48,9 @@ __global__ void __launch_bounds__(128) relay_build_kernel(const void* __restrict
   constexpr int LPR = D / 8;          // lanes per row
   constexpr int RPS = 32 / LPR;       // rows per warp step
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r = blockIdx.x;
+  const int r = blockIdx.x * 4 + warp;
   const int h = blockIdx.y, b = blockIdx.z;
+  if (r >= NB) return;
   const T* k = reinterpret_cast<const T*>(kp) + b * k_sb + h * k_sh;
   const T* v = reinterpret_cast<const T*>(vp) + b * v_sb + h * v_sh;
   const int row_lo = r * W;
@@ -62,24 +62,29 @@ __global__ void __launch_bounds__(128) relay_build_kernel(const void* __restrict
   for (int t = 0; t < 4; ++t) best[t] = Cand{-1.f, row_lo};
 
   if (R > 1) {
-    for (int i0 = row_lo + warp * RPS; i0 < row_hi; i0 += 4 * RPS) {
-      const int i = i0 + sub;
-      float acc = 0.f;
+    // lane-per-row scan: lane l takes rows row_lo + l, row_lo + l + 32, ...;
+    // all D/8 16-byte loads of a row are issued before use (the other half
+    // of each 32-byte sector comes from L1 on the lane's next load)
+    for (int i0 = row_lo; i0 < row_hi; i0 += 32) {
+      const int i = i0 + lane;
       if (i < row_hi) {
-        const uint4 u = *reinterpret_cast<const uint4*>(k + static_cast<int64_t>(i) * k_ss + part * 8);
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+        const uint4* rp = reinterpret_cast<const uint4*>(k + static_cast<int64_t>(i) * k_ss);
+        uint4 u[D / 8];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = E::unpack(w[e]);
-          acc = fmaf(f.x, f.x, acc);
-          acc = fmaf(f.y, f.y, acc);
+        for (int q = 0; q < D / 8; ++q) u[q] = rp[q];
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+        for (int q = 0; q < D / 8; ++q) {
+          const uint32_t w[4] = {u[q].x, u[q].y, u[q].z, u[q].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = E::unpack(w[e]);
+            a0 = fmaf(f.x, f.x, a0);
+            a1 = fmaf(f.y, f.y, a1);
+          }
         }
-      }
-#pragma unroll
-      for (int off = LPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-      if (i < row_hi && part == 0) {
-        Cand c{acc, i};
-        // insertion into the sorted top-4 list
+        Cand c{a0 + a1, i};
+        // insertion into this lane's sorted top-4 list
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
           if (better(c, best[t])) {
@@ -90,65 +95,28 @@ __global__ void __launch_bounds__(128) relay_build_kernel(const void* __restrict
         }
       }
     }
-    // merge the RPS row-group leaders' lists into lane 0
+    // merge the 32 lanes' lists (tree; the selection order is a total order,
+    // so the merge order does not matter), result in every lane
 #pragma unroll
-    for (int g = 1; g < RPS; ++g) {
+    for (int off = 16; off > 0; off >>= 1) {
       Cand in[4];
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
-        in[t].n = __shfl_sync(0xffffffffu, best[t].n, g * LPR);
-        in[t].i = __shfl_sync(0xffffffffu, best[t].i, g * LPR);
+        in[t].n = __shfl_xor_sync(0xffffffffu, best[t].n, off);
+        in[t].i = __shfl_xor_sync(0xffffffffu, best[t].i, off);
       }
-      if (lane == 0) {
 #pragma unroll
-        for (int t2 = 0; t2 < 4; ++t2) {
-          Cand c = in[t2];
+      for (int t2 = 0; t2 < 4; ++t2) {
+        Cand c = in[t2];
 #pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            if (better(c, best[t])) {
-              const Cand tmp = best[t];
-              best[t] = c;
-              c = tmp;
-            }
+        for (int t = 0; t < 4; ++t) {
+          if (better(c, best[t])) {
+            const Cand tmp = best[t];
+            best[t] = c;
+            c = tmp;
           }
         }
       }
-    }
-  }
-  // merge the four warps' lists (selection order is a total order: norm, then
-  // lower index, so merging in any order gives the same result)
-  __shared__ float s_n[4][4];
-  __shared__ int s_i[4][4];
-  if (R > 1 && lane == 0) {
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      s_n[warp][t] = best[t].n;
-      s_i[warp][t] = best[t].i;
-    }
-  }
-  __syncthreads();
-  if (warp != 0) return;
-  if (R > 1) {
-    if (lane == 0) {
-      for (int w2 = 1; w2 < 4; ++w2)
-#pragma unroll
-        for (int t2 = 0; t2 < 4; ++t2) {
-          Cand c{s_n[w2][t2], s_i[w2][t2]};
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            if (better(c, best[t])) {
-              const Cand tmp = best[t];
-              best[t] = c;
-              c = tmp;
-            }
-          }
-        }
-    }
-    // broadcast lane 0's result
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      best[t].n = __shfl_sync(0xffffffffu, best[t].n, 0);
-      best[t].i = __shfl_sync(0xffffffffu, best[t].i, 0);
     }
   }
 
@@ -196,7 +164,7 @@ cudaError_t launch_relay_build(int D, bool bf16, const void* k, const void* v, c
                                int B, int Hkv, int S, int W, int top_k, int R, int pos0, const float* log_scale,
                                void* gk, void* gv, int32_t* gsrc, cudaStream_t stream) {
   const int NB = (S + W - 1) / W;
-  dim3 grid(NB, Hkv, B);
+  dim3 grid((NB + 3) / 4, Hkv, B);
 #define CRA_RELAY(DD, BB)                                                                                          \
   relay_build_kernel<DD, BB><<<grid, 128, 0, stream>>>(k, v, ks[0], ks[1], ks[2], vs[0], vs[1], vs[2], Hkv, S, W, \
                                                        NB, top_k, R, pos0, log_scale, gk, gv, gsrc)
