@@ -74,18 +74,6 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Non-blocking probe of phase `parity` (never suspends the thread; for
-// polling several barriers from one thread).
-__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
 // CTA-wide abort state shared by all waits of one CTA.
 struct Abort {
   volatile int* flag;  // shared memory
@@ -140,10 +128,6 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
                : "memory");
 }
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
 // ---------------------------------------------------------------------------
 // TMEM + tcgen05
 // ---------------------------------------------------------------------------
@@ -183,27 +167,14 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool a
          ((b_mn ? 1u : 0u) << 16) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// MMA issue.  The whole warp executes these calls with warp-uniform operands
+// and one elected lane (always the same: the lowest) issues.  Issuing from a
+// converged warp keeps the descriptors on the uniform datapath; a lone thread
+// in a divergent branch sustains only about one MMA per ~90 cycles (measured
+// on B200), which caps M128 x N64 x K16 MMAs at about a third of the
+// tensor-core rate.  MMAs issued this way execute in issue order.
+//
 // D[tmem] (+)= A[smem] * B[smem]
-__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(accum)
-      : "memory");
-}
-// D[tmem] (+)= A[tmem] * B[smem]
-__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t accum) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accum)
-      : "memory");
-}
-// Warp-converged forms: the whole warp executes the call with warp-uniform
-// operands and one elected lane issues.  Issuing from a converged warp keeps
-// the descriptors on the uniform datapath; a lone thread in a divergent branch
-// sustains only about one MMA per ~90 cycles (measured on B200), which caps
-// M128 x N64 x K16 MMAs at about a third of the tensor-core rate.
 __device__ __forceinline__ void mma_ss_w(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
   asm volatile(
       "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
@@ -211,6 +182,7 @@ __device__ __forceinline__ void mma_ss_w(uint32_t d_tmem, uint64_t a, uint64_t b
       "l"(a), "l"(b), "r"(idesc), "r"(accum)
       : "memory");
 }
+// D[tmem] (+)= A[tmem] * B[smem]
 __device__ __forceinline__ void mma_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t accum) {
   asm volatile(
       "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
@@ -218,16 +190,13 @@ __device__ __forceinline__ void mma_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint6
       "r"(a_tmem), "l"(b), "r"(idesc), "r"(accum)
       : "memory");
 }
+// Arrive on `bar` once every MMA the elected lane issued so far has completed
+// (a commit covers all earlier MMAs of the thread, not just the latest).
 __device__ __forceinline__ void mma_commit_w(uint32_t bar) {
   asm volatile(
       "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
       "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(bar)
       : "memory");
-}
-
-// Arrive on `bar` once all previously issued tcgen05.mma of this thread finish.
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
 // 32 lanes x 32 columns of 32-bit: each thread gets 32 consecutive columns of
@@ -266,16 +235,6 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// Register re-allocation between warpgroups (warp-specialised kernels).
-template <int N>
-__device__ __forceinline__ void regs_dec() {
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
-}
-template <int N>
-__device__ __forceinline__ void regs_inc() {
-  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
-}
-
 // Packed two-lane fp32 arithmetic (one instruction for two values).
 // a = a * b + c on both lanes
 __device__ __forceinline__ void ffma2(float& a0, float& a1, float b, float c) {
@@ -290,13 +249,6 @@ __device__ __forceinline__ void fadd2(float& a0, float& a1, float b0, float b1) 
       "add.rn.f32x2 x, x, y;\n\tmov.b64 {%0, %1}, x;\n\t}"
       : "+f"(a0), "+f"(a1)
       : "f"(b0), "f"(b1));
-}
-// a *= b on both lanes
-__device__ __forceinline__ void fmul2(float& a0, float& a1, float b) {
-  asm("{\n\t.reg .b64 x, y;\n\tmov.b64 x, {%0, %1};\n\tmov.b64 y, {%2, %2};\n\t"
-      "mul.rn.f32x2 x, x, y;\n\tmov.b64 {%0, %1}, x;\n\t}"
-      : "+f"(a0), "+f"(a1)
-      : "f"(b));
 }
 
 // Hardware base-2 exponential (MUFU.EX2), flush-to-zero.  ex2(-inf) = +0.
@@ -348,11 +300,5 @@ struct Elt<false> {
   static __device__ __forceinline__ float to_f(T x) { return __half2float(x); }
   static __device__ __forceinline__ T from_f(float x) { return __float2half_rn(x); }
 };
-
-// Byte offset of 16-byte unit `u` (0..D/8-1) of row `r` inside a chunked,
-// 128B-swizzled [rows x D] tile (see the layout note at the top).
-__device__ __forceinline__ uint32_t sw128_off(int r, int u, int rows) {
-  return static_cast<uint32_t>((u >> 3) * rows * 128 + r * 128 + (((u & 7) ^ (r & 7)) << 4));
-}
 
 }  // namespace cra
