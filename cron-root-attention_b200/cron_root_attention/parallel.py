@@ -113,6 +113,8 @@ class LibcraShardOps:
 def _all_gather_padded(x: torch.Tensor, dim: int, sizes: Sequence[int], group) -> torch.Tensor:
     """Concatenate, along ``dim``, every rank's ``x`` (rank r contributes
     sizes[r] rows); pads to the largest size for the collective."""
+    if len(sizes) == 1:  # one rank: nothing to exchange
+        return x.narrow(dim, 0, sizes[0])
     mx = max(sizes)
     pad = mx - x.shape[dim]
     if pad:
@@ -134,10 +136,14 @@ def seq_parallel_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, seq_
     q, k, v: this rank's rows, [B, H, end - begin, D] with (begin, end) =
     seq_shard(seq_len, world, rank).  Returns this rank's output rows.
     Collectives: two all-gathers (global rows, then the halo rows); no
-    data-dependent host synchronisation.
+    data-dependent host synchronisation.  Without an initialized process
+    group (and no ``group`` given) it runs as a single rank.
     """
-    world = dist.get_world_size(group)
-    rank = dist.get_rank(group)
+    if group is None and not (dist.is_available() and dist.is_initialized()):
+        world, rank = 1, 0  # a single process: the whole sequence, no exchange
+    else:
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
     ops = ops or LibcraShardOps()
     begin, end = seq_shard(seq_len, world, rank)
     if q.shape[2] != end - begin or k.shape[2] != end - begin:

@@ -71,3 +71,19 @@ def test_seq_parallel_forward_gloo(world, S, tmp_path):
     q, k, v = (torch.randn(1, 2, S, 16, generator=g, dtype=torch.float64) for _ in range(3))
     ref, _ = O.forward(q, k, v, dtype=torch.float64)
     assert (o - ref).abs().max().item() < 1e-10
+
+
+@pytest.mark.parametrize("S", [3000, 1500])
+def test_seq_parallel_forward_without_process_group(S):
+    """No initialized process group: one rank holds the whole sequence and
+    nothing is exchanged."""
+    import torch.distributed as dist
+    from cron_root_attention.parallel import seq_parallel_forward
+    from oracle import cra_oracle as O
+    from shard_oracle import OracleShardOps
+    assert not (dist.is_available() and dist.is_initialized())
+    g = torch.Generator().manual_seed(7)
+    q, k, v = (torch.randn(1, 2, S, 16, generator=g, dtype=torch.float64) for _ in range(3))
+    o = seq_parallel_forward(q, k, v, S, ops=OracleShardOps())
+    ref, _ = O.forward(q, k, v, dtype=torch.float64)
+    assert (o - ref).abs().max().item() < 1e-10
