@@ -21,10 +21,13 @@ decomposition follows the attention's own structure (geom.cuh in libcra).
 """
 from __future__ import annotations
 
+import functools
+
 import ctypes
 import math
 from typing import Optional, Sequence, Tuple
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -58,15 +61,41 @@ def shard_units(batch: int, heads: int, world: int, rank: int) -> Sequence[Tuple
     return out
 
 
-def seq_shard(seq_len: int, world: int, rank: int) -> Tuple[int, int]:
-    """Query range [begin, end) of ``rank`` for a sequence split across
-    ``world`` ranks: W-blocks split as evenly as possible, block-aligned."""
+@functools.lru_cache(maxsize=64)
+def _shard_bounds(seq_len: int, world: int) -> Tuple[int, ...]:
+    """Block indices where each rank's W-blocks start (plus the end), chosen so
+    that every rank gets about the same attention work: a query m attends
+    min(m + 1, W) local keys and gcount(m) = R * floor(ls / W) + [ls % W != 0]
+    global rows (ls = max(m - W + 1, 0), R = 3 with the relay, else 1), so
+    later queries cost more and equal row counts would leave the last rank
+    with the most work."""
     W = window(seq_len)
     nb = (seq_len + W - 1) // W
     if nb < world:
         raise ValueError(f"{nb} W-blocks cannot be split across {world} ranks")
-    b0, b1 = nb * rank // world, nb * (rank + 1) // world
-    return b0 * W, min(b1 * W, seq_len)
+    R = 3 if seq_len > 2048 else 1
+    m = np.arange(seq_len, dtype=np.int64)
+    ls = np.maximum(m - W + 1, 0)
+    work = np.minimum(m + 1, W) + R * (ls // W) + (ls % W != 0)
+    per_block = np.add.reduceat(work, np.arange(0, seq_len, W))
+    cum = np.concatenate([[0], np.cumsum(per_block)]).astype(np.float64)
+    bounds = [0]
+    for r in range(1, world):
+        target = cum[-1] * r / world
+        blk = int(np.searchsorted(cum, target))  # first block boundary at or past the target
+        blk = min(max(blk, bounds[-1] + 1), nb - (world - r))  # every rank keeps >= 1 block
+        bounds.append(blk)
+    bounds.append(nb)
+    return tuple(bounds)
+
+
+def seq_shard(seq_len: int, world: int, rank: int) -> Tuple[int, int]:
+    """Query range [begin, end) of ``rank`` for a sequence split across
+    ``world`` ranks: block-aligned, contiguous, with about equal attention
+    work per rank (``_shard_bounds``)."""
+    W = window(seq_len)
+    bounds = _shard_bounds(seq_len, world)
+    return bounds[rank] * W, min(bounds[rank + 1] * W, seq_len)
 
 
 class LibcraShardOps:
@@ -166,8 +195,15 @@ def seq_parallel_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, seq_
     if rank > 0:
         off = sum(sizes[:rank - 1])
         n = sizes[rank - 1]
-        kk = torch.cat([hk.narrow(2, off, n), k], dim=2).contiguous()
-        vv = torch.cat([hv.narrow(2, off, n), v], dim=2).contiguous()
+        # halo rows in front of this rank's rows: one allocation and two plain
+        # copies each (a concatenation along the sequence dimension of
+        # GB-sized tensors ran far below HBM bandwidth)
+        kk = k.new_empty(k.shape[0], k.shape[1], n + k.shape[2], k.shape[3])
+        vv = v.new_empty(v.shape[0], v.shape[1], n + v.shape[2], v.shape[3])
+        kk[:, :, :n].copy_(hk.narrow(2, off, n))
+        kk[:, :, n:].copy_(k)
+        vv[:, :, :n].copy_(hv.narrow(2, off, n))
+        vv[:, :, n:].copy_(v)
         kv_begin = begin - n
     else:
         kk, vv, kv_begin = k.contiguous(), v.contiguous(), 0
