@@ -42,9 +42,22 @@ SEED = 2
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
+def visible_pairs(seq_len: int, top_k: int = 2) -> int:
+    """Exact visible (query, key) pairs per (b, h) for the FLOP count: local
+    window + strided keys + top_k relay rows per visible block, with
+    W = ceil(sqrt(S)) and the relay active for S > 2048."""
+    import math
+    W = math.isqrt(seq_len - 1) + 1 if seq_len > 1 else 1  # ceil(sqrt(S))
+    m = torch.arange(seq_len, dtype=torch.int64)
+    ls = (m - W + 1).clamp(min=0)
+    local = (m - ls + 1).sum().item()
+    strided = ((ls + W - 1) // W).sum().item()
+    relay = (top_k * (ls // W)).sum().item() if seq_len > 2048 else 0
+    return int(local + strided + relay)
+
+
 def pairs_per_head() -> int:
-    from oracle import cra_oracle as O  # pair counting only
-    return O.visible_pairs(S)
+    return visible_pairs(S)
 
 
 def flops():
@@ -350,7 +363,6 @@ def run_config(args, rank, world, local_rank):
         global rows and halo exchanged with NCCL all-gathers (strong scaling)."""
     import cron_root_attention as cra
     from cron_root_attention.parallel import seq_parallel_forward, seq_shard, shard_units
-    from oracle import cra_oracle as O
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     if args.config == "c4":
@@ -387,7 +399,7 @@ def run_config(args, rank, world, local_rank):
             t = torch.tensor([ms], device=dev, dtype=torch.float64)
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             ms = t.item()
-    f_fwd = 4.0 * Dc * O.visible_pairs(Sc) * Bc * Hc
+    f_fwd = 4.0 * Dc * visible_pairs(Sc) * Bc * Hc
     if rank == 0:
         print(json.dumps({"metric": METRIC, "config": {"workload": args.config, "B": Bc, "H": Hc, "S": Sc, "D": Dc,
                                                       "dtype": str(dt).replace("torch.", ""),
