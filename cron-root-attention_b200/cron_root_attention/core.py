@@ -247,7 +247,8 @@ def cron_root_attention_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor
                                relay_top_k: int = 2) -> torch.Tensor:
     """Packed variable-length forward (reference core.py:3836-3954): each
     document [cu_seqlens[i], cu_seqlens[i+1]) is attended independently.
-    ``cu_seqlens`` must be a CPU tensor or a Python sequence."""
+    ``cu_seqlens`` must be a CPU tensor or a Python sequence.  One call per
+    distinct document length (the reference makes one per document)."""
     if isinstance(cu_seqlens, torch.Tensor):
         if cu_seqlens.device.type != "cpu":
             raise ValueError("cu_seqlens must be a CPU tensor to avoid a device sync on each "
@@ -260,15 +261,26 @@ def cron_root_attention_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor
     if len(seqs) == 2:
         return cron_root_attention_v14(q, k, v, use_persistent=use_persistent, kv_groups=kv_groups,
                                        relay_log_scale=relay_log_scale, relay_top_k=relay_top_k)
-    parts = []
-    for s0, s1 in zip(seqs, seqs[1:]):
-        if s1 == s0:
-            continue
-        parts.append(cron_root_attention_v14(q.narrow(2, s0, s1 - s0), k.narrow(2, s0, s1 - s0),
-                                             v.narrow(2, s0, s1 - s0), use_persistent=use_persistent,
-                                             kv_groups=kv_groups, relay_log_scale=relay_log_scale,
-                                             relay_top_k=relay_top_k))
-    return torch.cat(parts, dim=2)
+    # Documents of equal length share W and the relay setting, so each such
+    # group runs as ONE batched call (documents stacked along the batch
+    # dimension) instead of one call per document: many short documents fill
+    # the GPU together.  Results are put back in document order.
+    docs = [(s0, s1 - s0) for s0, s1 in zip(seqs, seqs[1:]) if s1 > s0]
+    groups = {}
+    for s0, n in docs:
+        groups.setdefault(n, []).append(s0)
+    B = q.shape[0]
+    out = {}
+    for n, starts in groups.items():
+        if len(starts) == 1:
+            qs, ks, vs = (t.narrow(2, starts[0], n) for t in (q, k, v))
+        else:
+            qs, ks, vs = (torch.cat([t.narrow(2, s0, n) for s0 in starts], dim=0) for t in (q, k, v))
+        o = cron_root_attention_v14(qs, ks, vs, use_persistent=use_persistent, kv_groups=kv_groups,
+                                    relay_log_scale=relay_log_scale, relay_top_k=relay_top_k)
+        for i, s0 in enumerate(starts):
+            out[s0] = o.narrow(0, i * B, B)
+    return torch.cat([out[s0] for s0, _ in docs], dim=2)
 
 
 def warmup_varlen_shapes(doc_lengths, H: int, D: int, dtype=None, kv_groups: int = 1,

@@ -186,3 +186,27 @@ def test_varlen_matches_per_document(cuda_device):
         ref, _ = O.forward(q[:, :, s0:s1], k[:, :, s0:s1], v[:, :, s0:s1])
         _r = fwd_check(o[:, :, s0:s1], ref, torch.float16)
         assert _r["ok"], _r
+
+
+def test_varlen_equal_lengths_batched_matches_per_document(cuda_device):
+    """Equal-length documents go through one batched call: forward equals the
+    oracle, and forward and gradients equal separate per-document calls
+    bit for bit (every (b, h) is computed independently)."""
+    cra = _cra()
+    q, k, v = inputs(1, 2, 2, 3700, 64, torch.float16, 37)
+    cu = [0, 1024, 2048, 3072, 3700]
+    qd, kd, vd = (t.to(cuda_device).requires_grad_(True) for t in (q, k, v))
+    o = cra.cron_root_attention_varlen(qd, kd, vd, cu)
+    g = torch.randn(o.shape, generator=torch.Generator().manual_seed(3)).to(o)
+    (o * g).sum().backward()
+    for s0, s1 in zip(cu, cu[1:]):
+        ref, _ = O.forward(q[:, :, s0:s1], k[:, :, s0:s1], v[:, :, s0:s1])
+        _r = fwd_check(o[:, :, s0:s1], ref, torch.float16)
+        assert _r["ok"], _r
+        qs, ks, vs = (t[:, :, s0:s1].detach().clone().requires_grad_(True) for t in (qd, kd, vd))
+        os_ = cra.cron_root_attention(qs, ks, vs)
+        (os_ * g[:, :, s0:s1]).sum().backward()
+        assert torch.equal(os_, o[:, :, s0:s1])
+        assert torch.equal(qs.grad, qd.grad[:, :, s0:s1])
+        assert torch.equal(ks.grad, kd.grad[:, :, s0:s1])
+        assert torch.equal(vs.grad, vd.grad[:, :, s0:s1])
