@@ -14,10 +14,23 @@ batch (q, k, v and an upstream gradient dO), through the public API
 sparse TFLOP/s: 14 * D * visible pairs per (b, h) (4 forward + 10 backward);
 masked work done by a kernel is not counted.
 
+Beside the headline the same JSON line carries:
+  * per-kernel CUDA-event times of every kernel of the step (forward and
+    relay build through their C-ABI calls, the backward kernels through
+    cra_bwd_kernel_times), each against its roofline; ``roofline`` is the
+    kernel with the largest share of the step;
+  * BASELINE configs 4 and 5 (forward only, strong scaling): c4 = B1 H32
+    S262144 D128 fp16 with the heads split across the ranks, c5 = B1 H16
+    S524288 D128 bf16 with the one sequence split across the ranks (NCCL
+    all-gathers of the global rows and the halo).  Rank 0 first runs each
+    whole workload alone (the 1-GPU baseline), then every rank runs its
+    share; c5's split output is compared with the 1-GPU output.
+
 ``--impl reference`` times the reference's CPU algorithm for the same step
 (this repository's restatement of cpu_reference.cra_cpu_fast plus its
-autograd backward, oracle/cra_oracle.py) on the host cores, on a bounded
-sample (one of the 16 heads per step), and reports the same metric.
+autograd backward, oracle/cra_oracle.py) on the host cores.  Each of its
+steps is a bounded sample: the forward + backward of one (b, h) head of the
+16, heads taken in turn, so 16 steps cover one whole north-star step.
 """
 from __future__ import annotations
 
@@ -135,38 +148,114 @@ def make_inputs(rank: int, dev):
     return host, [t.to(dev) for t in host]
 
 
-def cpu_baseline(steps: int = 1):
-    """Restated reference CPU path (fp32) on one head: forward + backward."""
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_sample_steps(n_steps: int, n_warmup: int):
+    """Restated reference CPU path (fp32): each step is the forward + backward
+    of ONE (b, h) head, heads taken in turn (step i -> head i mod H), all host
+    threads.  Returns (seconds per step, steps timed, threads)."""
     from oracle import cra_oracle as O
-    g = torch.Generator().manual_seed(SEED)
-    q, k, v, do = (torch.randn(1, 1, S, D, generator=g).to(torch.bfloat16).float() for _ in range(4))
-    threads = torch.get_num_threads()
+    torch.set_num_threads(os.cpu_count() or 1)
+    heads = {}
+
+    def head(h):  # q, k, v, dO of head h (own seeded generator), drawn once
+        if h not in heads:
+            g = torch.Generator().manual_seed(SEED * 1000 + h)
+            heads[h] = tuple(torch.randn(1, 1, S, D, generator=g).to(torch.bfloat16).float() for _ in range(4))
+        return heads[h]
+
+    for i in range(n_warmup):
+        O.forward_backward(*head(i % H), dtype=torch.float32)
+    for i in range(min(n_steps, H)):
+        head(i)  # inputs drawn outside the timed region
     t0 = time.perf_counter()
-    for _ in range(steps):
-        O.forward_backward(q, k, v, do, dtype=torch.float32)
-    dt = (time.perf_counter() - t0) / steps
+    for i in range(n_steps):
+        O.forward_backward(*head(i % H), dtype=torch.float32)
+    return (time.perf_counter() - t0) / n_steps, n_steps, torch.get_num_threads()
+
+
+def cpu_baseline_line(per_step_s: float, n: int, threads: int) -> dict:
     f = 14.0 * D * pairs_per_head()  # one head
-    return {"value": f / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-            "sample": f"1 of {H} heads per step (B1 S{S} D{D}), fp32 restatement of cpu_reference.cra_cpu_fast "
-                      f"+ autograd backward, {dt:.2f} s per head"}
+    return {"value": f / per_step_s / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "cpu_model": cpu_model(), "host_cpus": os.cpu_count(),
+            "sample": f"{n} steps, each the fwd+bwd of one of the {H} heads of B1 S{S} D{D} (heads in turn), "
+                      f"fp32 restatement of cpu_reference.cra_cpu_fast + autograd backward, "
+                      f"{per_step_s:.2f} s per head = {per_step_s * H:.1f} s per whole {H}-head step"}
 
 
 def run_reference(args, rank, world):
+    """The reference's CPU algorithm (restated, oracle/cra_oracle.py) on the
+    host cores.  Rank 0 alone works; other ranks exit without work."""
     if rank != 0:
         return
-    torch.set_num_threads(os.cpu_count() or 1)
-    for _ in range(args.warmup):
-        pass  # the CPU path has no warm-up state worth timing; a sample per step below
-    cb = cpu_baseline(steps=max(1, min(args.steps, 3)))
-    ms = 14.0 * D * pairs_per_head() * H / (cb["value"] * 1e12) * 1e3  # full step = 16 heads
+    n = max(1, min(args.steps, 24))  # bounded: about 3 s per step on 16 cores
+    per, n, threads = cpu_sample_steps(n, min(args.warmup, 3))
+    cb = cpu_baseline_line(per, n, threads)
     line = {"metric": METRIC, "impl": "reference", "value": cb["value"], "unit": "TFLOP/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"fwd+bwd B{B} H{H} S{S} D{D} (CPU sample: one head per step)",
-                       "seq_len": S, "heads": H, "head_dim": D, "global_batch": B},
+            "steps": n, "steps_requested": args.steps, "warmup": min(args.warmup, 3), "ms_per_step": per * 1e3,
+            "ms_per_full_step": per * H * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"fwd+bwd B{B} H{H} S{S} D{D}; one step = one head's fwd+bwd (bounded "
+                                   f"sample), heads in turn", "seq_len": S, "heads": H, "head_dim": D,
+                       "global_batch": B},
             "cpu_baseline": cb,
             "e2e": {"value": cb["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of each
+# kernel, from one ncu capture of the committed kernels at B1 H8 S65536 D128
+# bf16, scaled by H / 8 (every kernel's traffic grows in proportion to the
+# heads).  None where no capture of the current kernel exists.
+TRAFFIC_H8 = {
+    "fwd_kernel": None,
+    "relay_build_kernel": None,
+    "delta_kernel": None,
+    "keyglobal_kernel": None,
+    "reduce_kernel": None,
+    "keylocal_kernel": None,
+    "dq_kernel": None,
+}
+
+
+def kernel_work(name: str, W: int, NG: int):
+    """(bound, algorithmic work per launch, unit) of each kernel at B x H x S x D.
+    Attention kernels: the useful (unmasked) MMA FLOPs they perform -- 2 D per
+    visible pair per GEMM; forward 2 GEMMs, dQ pass 3 (S, dP, dQ), key passes
+    4 (S, dP, dV, dK) over their own pairs.  HBM kernels: bytes they must
+    move."""
+    import math
+    m = torch.arange(S, dtype=torch.int64)
+    ls = (m - W + 1).clamp(min=0)
+    local = int((m - ls + 1).sum())
+    glob = pairs_per_head() - local
+    bh = B * H
+    eb = 2
+    if name == "fwd_kernel":
+        return "tensor", 4.0 * D * pairs_per_head() * bh, "TFLOP/s"
+    if name == "dq_kernel":
+        return "tensor", 6.0 * D * pairs_per_head() * bh, "TFLOP/s"
+    if name == "keyglobal_kernel":
+        return "tensor", 8.0 * D * glob * bh, "TFLOP/s"
+    if name == "keylocal_kernel":
+        return "tensor", 8.0 * D * local * bh, "TFLOP/s"
+    if name == "relay_build_kernel":  # K read once + chosen K / V rows read and written as G
+        return "hbm", (S * D * eb + 4 * NG * D * eb) * bh, "GB/s"
+    if name == "delta_kernel":  # O, dO read; lse read; lse2, delta written (fp32, padded)
+        spad = math.ceil(S / 128) * 128
+        return "hbm", (2 * S * D * eb + 4 * S + 8 * spad) * bh, "GB/s"
+    if name == "reduce_kernel":  # n_split partials of dG_k, dG_v read, dG written (fp32)
+        return "hbm", None, "GB/s"
+    return "other", None, None
 
 
 def run_ours(args, rank, world, local_rank):
@@ -235,8 +324,7 @@ def run_ours(args, rank, world, local_rank):
     with torch.no_grad():
         ms_fwd = timed(lambda: cra.cron_root_attention(q, k, v), args.steps)
 
-    # --- dominant kernel, timed alone through the C ABI on this stream:
-    # the attention forward kernel (cra_fwd launches exactly one kernel)
+    # --- every kernel of the step, timed alone with CUDA events on this stream
     L = _lib.lib()
     W = L.cra_window(S)
     NG = L.cra_global_rows(S, 1, 2)
@@ -248,17 +336,37 @@ def run_ours(args, rank, world, local_rank):
     lse = torch.empty(B, H, S, device=dev, dtype=torch.float32)
     st = _lib.strides3
     sp = stream.cuda_stream
-    _lib.check(L.cra_relay_build(k.data_ptr(), v.data_ptr(), st(k), st(v), B, H, S, D, 1, 1, 2, None,
-                                 gk.data_ptr(), gv.data_ptr(), gsrc.data_ptr(), sp), "relay")
+    err = _err_word(dev).data_ptr()
+    args_relay = (k.data_ptr(), v.data_ptr(), st(k), st(v), B, H, S, D, 1, 1, 2, None, gk.data_ptr(), gv.data_ptr(),
+                  gsrc.data_ptr(), sp)
+    _lib.check(L.cra_relay_build(*args_relay), "relay")
     args_fwd = (q.data_ptr(), k.data_ptr(), v.data_ptr(), gk.data_ptr(), gv.data_ptr(), st(q), st(k), st(v),
-                B, H, H, S, D, 1, 1, 2, ctypes.c_float(D ** -0.5), o.data_ptr(), st(o), lse.data_ptr(),
-                _err_word(dev).data_ptr(), sp)
+                B, H, H, S, D, 1, 1, 2, ctypes.c_float(D ** -0.5), o.data_ptr(), st(o), lse.data_ptr(), err, sp)
     for _ in range(3):
         L.cra_fwd(*args_fwd)
-    ms_kernel = timed(lambda: L.cra_fwd(*args_fwd), args.steps)
-    ms_relay = timed(lambda: L.cra_relay_build(k.data_ptr(), v.data_ptr(), st(k), st(v), B, H, S, D, 1, 1, 2,
-                                               None, gk.data_ptr(), gv.data_ptr(), gsrc.data_ptr(), sp),
-                     args.steps)
+    kern_ms = {"fwd_kernel": timed(lambda: L.cra_fwd(*args_fwd), args.steps),
+               "relay_build_kernel": timed(lambda: L.cra_relay_build(*args_relay), args.steps)}
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    ws_bytes = L.cra_bwd_workspace_bytes(B, H, H, S, D, 1, 2)
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    nmax = 8
+    ms_arr = (ctypes.c_float * nmax)()
+    names = (ctypes.c_char_p * nmax)()
+    nk = ctypes.c_int(0)
+    samples = {}
+    for it in range(3 + args.steps):
+        _lib.check(L.cra_bwd_kernel_times(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(), lse.data_ptr(), gk.data_ptr(),
+            gv.data_ptr(), gsrc.data_ptr(), st(q), st(k), st(v), st(o), st(do), B, H, H, S, D, 1, 1, 2,
+            ctypes.c_float(D ** -0.5), None, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), st(dq), st(dk), st(dv),
+            None, ws.data_ptr(), ws_bytes, err, sp, ms_arr, names, nmax, ctypes.byref(nk)), "cra_bwd_kernel_times")
+        if it >= 3:
+            for i in range(nk.value):
+                samples.setdefault(names[i].decode(), []).append(ms_arr[i])
+    for name, xs in samples.items():
+        kern_ms[name] = max_over_ranks(statistics.median(xs))
+    n_bwd_kernels = nk.value
+    del ws, dq, dk, dv
 
     # --- end to end through the public API with host buffers: every step copies
     # q, k, v, dO from pinned memory to the device, runs fwd + bwd, and copies
@@ -306,18 +414,40 @@ def run_ours(args, rank, world, local_rank):
     n_e2e = max(2, min(args.steps, 8))
     ms_e2e = timed(lambda: e2e_run(n_e2e), 1) / n_e2e
     nbytes = host[0].numel() * host[0].element_size()
+    del dev_in, out_host, host, gk, gv, gsrc, o, lse
 
     assert cra.check_device_errors(dev) == 0, "a kernel gave up on a bounded wait"
+
+    extra = {}
+    if not args.no_strong:
+        del q, k, v, do
+        torch.cuda.empty_cache()
+        for cfg in ("c4", "c5"):
+            extra.update(strong_config(cfg, args, rank, world, local_rank))
+        assert cra.check_device_errors(dev) == 0, "a kernel gave up on a bounded wait"
 
     if rank != 0:
         return
     peaks, peak_src = load_peaks()
-    achieved = f_fwd / (ms_kernel * 1e-3) / 1e12
-    peak = float(peaks["bf16_tflops"])
-    # DRAM bytes per forward launch: ncu dram__bytes_read.sum + write.sum of one
-    # launch at H = 8 (profiles/kernels_northstar_h8.md: 405.9 + 117.1 MB),
-    # scaled by H / 8 (the traffic grows in proportion to the heads)
-    traffic = (405.935360e6 + 119.967488e6) * (H / 8) if (S, D) == (65536, 128) else None
+    kernels = {}
+    for name, ms in kern_ms.items():
+        bound, work, unit = kernel_work(name, W, NG)
+        ent = {"ms": ms, "share_of_step": ms / ms_step}
+        if work is not None:
+            if bound == "tensor":
+                ach, peak = work / (ms * 1e-3) / 1e12, float(peaks["bf16_tflops"])
+            else:
+                ach, peak = work / (ms * 1e-3) / 1e9, float(peaks["hbm_gbs"])
+            ent.update({"bound": bound, "achieved": ach, "peak": peak, "unit": unit, "frac": ach / peak})
+        t8 = TRAFFIC_H8.get(name)
+        ent["traffic"] = t8 * (H / 8) if (t8 is not None and (S, D) == (65536, 128)) else None
+        kernels[name] = ent
+    top = max((n for n in kernels if "frac" in kernels[n]), key=lambda n: kernels[n]["ms"])
+    kt = kernels[top]
+    roofline = {"kernel": top, "bound": kt["bound"], "achieved": kt["achieved"], "peak": kt["peak"],
+                "unit": kt["unit"], "frac": kt["frac"], "traffic": kt["traffic"],
+                "peak_source": f"{peak_src} " + ("bf16 dense (burst)" if kt["bound"] == "tensor" else "HBM copy"),
+                "kernel_ms": kt["ms"]}
     line = {
         "metric": METRIC,
         "value": world * (f_fwd + f_bwd) / (ms_step * 1e-3) / 1e12,
@@ -338,87 +468,139 @@ def run_ours(args, rank, world, local_rank):
                    "parallelism": f"batch-sharded x{world}, no data-path collective",
                    "l2": "inputs larger than L2 (each of q, k, v, dO is 268 MB; L2 126 MB)",
                    "flops_per_step": f"fwd {f_fwd / 1e9:.3f} GFLOP + bwd {f_bwd / 1e9:.3f} GFLOP per GPU"},
-        "roofline": {"kernel": "fwd_kernel<128,bf16>", "bound": "tensor", "achieved": achieved, "peak": peak,
-                     "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
-                     "peak_source": f"{peak_src} bf16 dense (burst)", "kernel_ms": ms_kernel,
-                     "relay_build_ms": ms_relay,
-                     # K read once (norms) + the chosen K / V rows read and written as G
-                     "relay_build_gbs": (B * H * S * D * 2 + 4 * B * H * NG * D * 2) / (ms_relay * 1e-3) / 1e9},
+        "roofline": roofline,
+        "kernels": kernels,
         "e2e": {"value": world * (f_fwd + f_bwd) / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
                 "ms_per_step": ms_e2e, "h2d_bytes_per_step": 4 * nbytes, "d2h_bytes_per_step": 3 * nbytes,
-                "steps": n_e2e, "copies": "pipelined across steps on separate H2D / D2H streams"},
-        "gpu_launches": 7 * args.steps,
+                "steps": n_e2e, "copies": "pipelined across steps on separate H2D / D2H streams",
+                "limit": "host copies: 1.07 GB up + 0.81 GB down per step per GPU over PCIe; at N > 1 every "
+                         "GPU's copies share the host's memory path"},
+        # our kernels per timed step: relay build + forward, then the backward's
+        # kernels as cra_bwd_kernel_times reported them
+        "gpu_launches": (2 + n_bwd_kernels) * args.steps,
         "clocks": clocks,
     }
+    line.update(extra)
     if world == 1:
-        line["cpu_baseline"] = cpu_baseline()
+        per, n, threads = cpu_sample_steps(1, 0)
+        line["cpu_baseline"] = cpu_baseline_line(per, n, threads)
     print(json.dumps(line), flush=True)
 
 
-def run_config(args, rank, world, local_rank):
-    """BASELINE configs 4 and 5 (forward only, multi-GPU):
-    c4: B1 H32 D128 S262144 fp16, heads split evenly across ranks, no collective
-        (strong scaling: the total work is fixed);
-    c5: B1 H16 D128 S524288 bf16, one sequence split by W-blocks across ranks,
-        global rows and halo exchanged with NCCL all-gathers (strong scaling)."""
+STRONG = {  # BASELINE configs 4 and 5: (B, H, S, D, dtype, seed, sigma)
+    "c4": (1, 32, 262144, 128, torch.float16, 3, 0.5),
+    "c5": (1, 16, 524288, 128, torch.bfloat16, 4, 1.0),
+}
+
+
+def strong_config(cfg: str, args, rank: int, world: int, local_rank: int) -> dict:
+    """Forward of BASELINE config 4 (heads split across ranks) or 5 (one
+    sequence split across ranks), strong scaling.  Inputs are drawn on the
+    device from a seeded generator (the same values on every rank).  Rank 0
+    first times the whole workload alone on its GPU (the 1-GPU baseline);
+    then every rank runs its share, timed between barriers, max over ranks.
+    c5 at N > 1 also gathers head 0 of the split output and compares it with
+    the 1-GPU output (same kernel, different query-tile boundaries)."""
     import cron_root_attention as cra
     from cron_root_attention.parallel import seq_parallel_forward, seq_shard, shard_units
     dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
-    if args.config == "c4":
-        Bc, Hc, Sc, Dc, dt, seed, sig = 1, 32, 262144, 128, torch.float16, 3, 0.5
-    else:
-        Bc, Hc, Sc, Dc, dt, seed, sig = 1, 16, 524288, 128, torch.bfloat16, 4, 1.0
-    g = torch.Generator().manual_seed(seed)
-    if args.config == "c4":
-        (b, h0, h1), = shard_units(Bc, Hc, world, rank)
-        # each rank draws only its own heads' rows: the same values as slicing the full tensors
-        q, k, v = (torch.randn(Bc, Hc, Sc, Dc, generator=g)[:, h0:h1].mul_(sig).to(dt).to(dev) for _ in range(3))
-        fn = lambda: cra.cron_root_attention(q, k, v)
-    else:
-        s0, s1 = seq_shard(Sc, world, rank)
-        q, k, v = (torch.randn(Bc, Hc, Sc, Dc, generator=g)[:, :, s0:s1].mul_(sig).to(dt).to(dev) for _ in range(3))
-        fn = lambda: seq_parallel_forward(q, k, v, Sc)
-    with torch.no_grad():
-        for _ in range(max(args.warmup, 3)):
-            fn()
-        torch.cuda.synchronize(dev)
+    Bc, Hc, Sc, Dc, dt, seed, sig = STRONG[cfg]
+    g = torch.Generator(device=dev).manual_seed(seed)
+    q, k, v = (torch.randn(Bc, Hc, Sc, Dc, generator=g, device=dev).mul_(sig).to(dt) for _ in range(3))
+    steps = max(3, min(args.steps, 20))
+
+    def run_timed(fn, n, ranks_all: bool):
         if world > 1:
             torch.distributed.barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        with ClockSampler(local_rank) as clk:
-            time.sleep(0.6)
-            e0.record()
-            for _ in range(args.steps):
-                fn()
-            e1.record()
-            torch.cuda.synchronize(dev)
-        ms = e0.elapsed_time(e1) / args.steps
-        if world > 1:
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / n
+        if world > 1 and ranks_all:
             t = torch.tensor([ms], device=dev, dtype=torch.float64)
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             ms = t.item()
-    f_fwd = 4.0 * Dc * visible_pairs(Sc) * Bc * Hc
+        return ms
+
+    out = {}
+    with torch.no_grad():
+        # 1-GPU baseline: rank 0, whole workload
+        ms1, ref0 = None, None
+        if rank == 0:
+            whole = lambda: cra.cron_root_attention(q, k, v)
+            for _ in range(3):
+                whole()
+            ms1 = run_timed(whole, steps, False) if world == 1 else None
+            if world > 1:  # time it alone while the other ranks wait at the barrier below
+                torch.cuda.synchronize(dev)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(steps):
+                    whole()
+                e1.record()
+                torch.cuda.synchronize(dev)
+                ms1 = e0.elapsed_time(e1) / steps
+            if cfg == "c5" and world > 1:
+                ref0 = whole()[:, 0].float()
+        if world > 1:
+            # the split run
+            if cfg == "c4":
+                (b, h0, h1), = shard_units(Bc, Hc, world, rank)
+                qs, ks, vs = (t[:, h0:h1].contiguous() for t in (q, k, v))
+                fn = lambda: cra.cron_root_attention(qs, ks, vs)
+            else:
+                s0, s1 = seq_shard(Sc, world, rank)
+                qs, ks, vs = (t[:, :, s0:s1].contiguous() for t in (q, k, v))
+                fn = lambda: seq_parallel_forward(qs, ks, vs, Sc)
+            del q, k, v
+            for _ in range(3):
+                fn()
+            with ClockSampler(local_rank) as clk:
+                time.sleep(0.3)
+                msN = run_timed(fn, steps, True)
+            if cfg == "c5":
+                o = fn()[:, 0].float().contiguous()
+                s0s1 = [seq_shard(Sc, world, r) for r in range(world)]
+                mx = max(e - b for b, e in s0s1)
+                buf = torch.zeros(Bc, mx, Dc, device=dev)
+                buf[:, :o.shape[1]] = o
+                parts = [torch.empty_like(buf) for _ in range(world)]
+                torch.distributed.all_gather(parts, buf)
+                if rank == 0:
+                    split = torch.cat([p[:, :e - b] for p, (b, e) in zip(parts, s0s1)], dim=1)
+                    diff = (split - ref0).abs()
+                    bar = 2e-3 + 2.0 ** -7 * (ref0.abs() + 1.0)  # one bf16 ulp of the output scale
+                    out["c5_vs_1gpu"] = {"head": 0, "max_abs": diff.max().item(), "mean_abs": diff.mean().item(),
+                                         "parity_ok": bool((diff <= bar).all().item())}
+        else:
+            msN = ms1
+            clk = None
     if rank == 0:
-        print(json.dumps({"metric": METRIC, "config": {"workload": args.config, "B": Bc, "H": Hc, "S": Sc, "D": Dc,
-                                                      "dtype": str(dt).replace("torch.", ""),
-                                                      "parallelism": ("heads" if args.config == "c4" else "sequence")
-                                                      + f" split x{world}"},
-                          "value": f_fwd / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms, "n_gpus": world,
-                          "steps": args.steps, "scaling": "strong", "clocks": clk.summary()}), flush=True)
+        f = 4.0 * Dc * visible_pairs(Sc) * Bc * Hc
+        out.update({f"{cfg}_ms": msN, f"{cfg}_ms_1gpu": ms1, f"{cfg}_speedup_vs_1": ms1 / msN,
+                    f"{cfg}_tflops": f / (msN * 1e-3) / 1e12,
+                    f"{cfg}_config": {"B": Bc, "H": Hc, "S": Sc, "D": Dc, "dtype": str(dt).replace("torch.", ""),
+                                      "pass": "forward", "scaling": "strong",
+                                      "parallelism": ("heads" if cfg == "c4" else "sequence") + f" split x{world}",
+                                      "data": "synthetic, seeded on the device"}})
+        if clk is not None:
+            out[f"{cfg}_clocks"] = clk.summary()
+    return out
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--mode", default="all", choices=["all", "fwd", "fwdbwd"],
                     help="fwd / fwdbwd: time only that pass (for profiling runs)")
-    ap.add_argument("--config", default="northstar", choices=["northstar", "c4", "c5"],
-                    help="c4 / c5: BASELINE configs 4 and 5 (forward, strong scaling over --gpus)")
+    ap.add_argument("--no-strong", action="store_true", help="skip the config 4 / 5 strong-scaling legs")
     ap.add_argument("--heads", type=int, default=H)
     ap.add_argument("--seq", type=int, default=S)
     args = ap.parse_args()
@@ -434,8 +616,6 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
-        elif args.config != "northstar":
-            run_config(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)
     finally:

@@ -5,6 +5,9 @@
 Compiles every ``csrc/*.cu`` to an object (skipped when up to date) and links
 them into ``cron_root_attention/libcra.so`` (CUDA runtime linked statically;
 the driver is reached through cudaGetDriverEntryPoint, so no -lcuda).
+Also builds the test-only ``cron_root_attention/libcra_waitprobe.so`` from
+``csrc/testing/wait_probe.cu`` with a 0.2 ms wait limit (used by the failure
+handling tests, never by the package).
 """
 import glob
 import os
@@ -15,6 +18,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OBJ = os.path.join(HERE, "_build")
 OUT = os.path.join(HERE, "cron_root_attention", "libcra.so")
+PROBE_SRC = os.path.join(CSRC, "testing", "wait_probe.cu")
+PROBE_OUT = os.path.join(HERE, "cron_root_attention", "libcra_waitprobe.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17",
          "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden"]
@@ -42,6 +47,11 @@ def build(force: bool = False, verbose: bool = True) -> str:
         objs.append(o)
     if force or _newer(objs, OUT):
         cmd = [NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", OUT] + objs
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.check_call(cmd)
+    if force or _newer([PROBE_SRC] + headers, PROBE_OUT):
+        cmd = [NVCC] + FLAGS + ["-DCRA_WAIT_LIMIT_NS=200000ull", "-shared", PROBE_SRC, "-o", PROBE_OUT]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.check_call(cmd)

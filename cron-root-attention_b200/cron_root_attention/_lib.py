@@ -42,6 +42,10 @@ _SIGNATURES = {
     "cra_bwd": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _i64p, _i64p,
                      _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _vp, _vp,
                      ctypes.c_size_t, _vp, _vp]),
+    "cra_bwd_kernel_times": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _i64p, _i64p,
+                                  _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _vp,
+                                  _vp, ctypes.c_size_t, _vp, _vp, ctypes.POINTER(_f),
+                                  ctypes.POINTER(ctypes.c_char_p), _i, ctypes.POINTER(_i)]),
     "cra_bwd_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _i64p, _i64p,
                              _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _vp,
                              _vp, _vp]),

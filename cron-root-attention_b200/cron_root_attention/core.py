@@ -24,6 +24,7 @@ from __future__ import annotations
 
 import ctypes
 import math
+import os
 from functools import lru_cache
 from typing import Optional, Sequence, Union
 
@@ -70,8 +71,13 @@ def get_num_sms() -> int:
 
 # ---------------------------------------------------------------------------
 # per-device error word: kernels record a timed-out wait here instead of
-# trapping; ``check_device_errors`` reads it.
+# trapping; ``check_device_errors`` reads it.  A kernel that gave up on a wait
+# leaves its outputs partly written, so a caller that cannot rule that out
+# polls ``check_device_errors`` at a convenient point (for example once per
+# training step), or sets CRA_CHECK_DEVICE_ERRORS=1 to have every forward and
+# backward call synchronize and raise RuntimeError when the word is set.
 _ERR_WORDS: dict = {}
+_CHECK_EACH_CALL = os.environ.get("CRA_CHECK_DEVICE_ERRORS", "0") not in ("", "0")
 
 
 def _err_word(device: torch.device) -> torch.Tensor:
@@ -85,13 +91,26 @@ def _err_word(device: torch.device) -> torch.Tensor:
 
 def check_device_errors(device: Optional[torch.device] = None, reset: bool = True) -> int:
     """Return (and by default clear) the device error word of ``device``.
-    0 = no kernel gave up on a bounded wait since the last check."""
+    0 = no kernel gave up on a bounded wait since the last check; 1
+    (CRA_DEV_WAIT_TIMEOUT) = some kernel did, and the outputs of the calls
+    since the last check are not to be trusted.  Reading the word
+    synchronizes the device."""
     device = device or torch.device("cuda", torch.cuda.current_device())
     t = _err_word(device)
     v = int(t.item())
     if reset and v:
         t.zero_()
     return v
+
+
+def _raise_on_device_error(device: torch.device, what: str) -> None:
+    """With CRA_CHECK_DEVICE_ERRORS set: synchronize and raise when a kernel of
+    ``what`` (or an earlier unchecked call) gave up on a bounded wait."""
+    if _CHECK_EACH_CALL:
+        code = check_device_errors(device)
+        if code:
+            raise RuntimeError(f"cron_root_attention {what}: a kernel gave up on a bounded device wait "
+                               f"(device error {code}); its outputs are incomplete")
 
 
 def _dtype_code(dt: torch.dtype) -> int:
@@ -180,6 +199,7 @@ class CronRootAttentionV14Function(torch.autograd.Function):
         with torch.cuda.device(dev):
             o, lse = _launch_fwd(L, qc, kc, vc, gk, gv, gsrc, alpha, B, Hq, Hkv, S, Dp, cdt, use_relay,
                                  relay_top_k, scale, dev, stream)
+        _raise_on_device_error(dev, "forward")
         ctx.save_for_backward(qc, kc, vc, o, lse, gk, gv, gsrc, alpha)
         ctx.meta = (B, Hq, Hkv, S, D, Dp, use_relay, relay_top_k, scale, in_dtype, cdt,
                     relay_log_scale is not None)
@@ -211,6 +231,7 @@ class CronRootAttentionV14Function(torch.autograd.Function):
                             dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), strides3(dq), strides3(dk), strides3(dv),
                             dalpha.data_ptr() if dalpha is not None else None,
                             ws.data_ptr(), ws_bytes, _err_word(dev).data_ptr(), stream), "cra_bwd")
+        _raise_on_device_error(dev, "backward")
 
         def fin(t):
             t = t if Dp == D else t[..., :D]

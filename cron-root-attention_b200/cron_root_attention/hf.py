@@ -14,8 +14,12 @@ model family through ``fn``.  This module provides that ``fn``:
     model = AutoModelForCausalLM.from_config(cfg, attn_implementation="cron_root")
 
 Semantics are the reference patch's: the attention is causal by
-construction, so the model's mask is not used (transformers builds none for a
-custom implementation name); grouped K/V heads go to the kernels natively
+construction.  The model's mask is checked, not applied: a mask that only
+restates causality (or none, which transformers passes when the batch has no
+padding) is accepted; a mask that hides any key a causal query would see --
+padding in a batch, packed documents -- raises ``NotImplementedError``, since
+the kernels cannot honour it and silently ignoring it would give wrong
+outputs.  Grouped K/V heads go to the kernels natively
 (``kv_groups = H_q / H_kv``) instead of being expanded.  A model scaling other
 than 1/sqrt(head_dim) is folded into q.  Unsupported, raising
 ``NotImplementedError``: attention dropout while training, a KV cache whose
@@ -32,6 +36,20 @@ import torch
 from . import core as _core
 
 ATTN_NAME = "cron_root"
+
+
+def _hides_causal_keys(mask: torch.Tensor, S: int) -> bool:
+    """True when ``mask`` masks out some (query i, key j <= i) pair.  Accepts
+    a [B, S] keep-mask (1 = token present), or a [B, 1|H, S, S_k] boolean
+    (True = attend) or additive float (0 = attend, large negative = masked)
+    mask whose last S key columns align with the queries."""
+    if mask.dim() == 2:  # padding mask
+        return bool((mask[:, -S:] == 0).any())
+    m = mask[..., -S:, -S:]
+    tril = torch.ones(S, S, dtype=torch.bool, device=m.device).tril()
+    if m.dtype == torch.bool:
+        return bool((~m & tril).any())
+    return bool(((m < -1e4) & tril).any())
 
 
 def cron_root_attention_forward(module: torch.nn.Module, query: torch.Tensor, key: torch.Tensor,
@@ -51,6 +69,10 @@ def cron_root_attention_forward(module: torch.nn.Module, query: torch.Tensor, ke
     if query.dim() != 4 or key.dim() != 4 or value.dim() != 4:
         raise ValueError("expected [B, H, S, D] query / key / value")
     B, Hq, S, D = query.shape
+    if attention_mask is not None and _hides_causal_keys(attention_mask, S):
+        raise NotImplementedError(
+            "cron_root attention is causal only: the attention mask hides keys a causal query would see "
+            "(padding or packed documents); use unpadded batches, or cron_root_attention_varlen for packing")
     Hkv = key.shape[1]
     if key.shape[2] != S or value.shape[2] != S:
         raise NotImplementedError(

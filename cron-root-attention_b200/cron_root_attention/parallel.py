@@ -62,18 +62,19 @@ def shard_units(batch: int, heads: int, world: int, rank: int) -> Sequence[Tuple
 
 
 @functools.lru_cache(maxsize=64)
-def _shard_bounds(seq_len: int, world: int) -> Tuple[int, ...]:
+def _shard_bounds(seq_len: int, world: int, top_k: int = 2) -> Tuple[int, ...]:
     """Block indices where each rank's W-blocks start (plus the end), chosen so
     that every rank gets about the same attention work: a query m attends
     min(m + 1, W) local keys and gcount(m) = R * floor(ls / W) + [ls % W != 0]
-    global rows (ls = max(m - W + 1, 0), R = 3 with the relay, else 1), so
+    global rows (ls = max(m - W + 1, 0), R = 1 + top_k with the relay, else
+    1), so
     later queries cost more and equal row counts would leave the last rank
     with the most work."""
     W = window(seq_len)
     nb = (seq_len + W - 1) // W
     if nb < world:
         raise ValueError(f"{nb} W-blocks cannot be split across {world} ranks")
-    R = 3 if seq_len > 2048 else 1
+    R = 1 + top_k if seq_len > 2048 else 1
     m = np.arange(seq_len, dtype=np.int64)
     ls = np.maximum(m - W + 1, 0)
     work = np.minimum(m + 1, W) + R * (ls // W) + (ls % W != 0)
@@ -89,12 +90,12 @@ def _shard_bounds(seq_len: int, world: int) -> Tuple[int, ...]:
     return tuple(bounds)
 
 
-def seq_shard(seq_len: int, world: int, rank: int) -> Tuple[int, int]:
+def seq_shard(seq_len: int, world: int, rank: int, top_k: int = 2) -> Tuple[int, int]:
     """Query range [begin, end) of ``rank`` for a sequence split across
     ``world`` ranks: block-aligned, contiguous, with about equal attention
-    work per rank (``_shard_bounds``)."""
+    work per rank (``_shard_bounds``) for ``top_k`` relay tokens per block."""
     W = window(seq_len)
-    bounds = _shard_bounds(seq_len, world)
+    bounds = _shard_bounds(seq_len, world, top_k)
     return bounds[rank] * W, min(bounds[rank + 1] * W, seq_len)
 
 
@@ -112,7 +113,11 @@ class LibcraShardOps:
         gk = torch.empty(B, Hkv, nblk * R, D, device=k.device, dtype=k.dtype)
         gv = torch.empty_like(gk)
         gsrc = torch.empty(B, Hkv, nblk, top_k, device=k.device, dtype=torch.int32)
-        alpha = relay_log_scale.float().contiguous() if relay_log_scale is not None else None
+        alpha = None
+        if relay_log_scale is not None and use_relay:
+            alpha = relay_log_scale.detach().to(device=k.device, dtype=torch.float32).contiguous()
+            if alpha.numel() != Hkv:
+                raise ValueError(f"relay_log_scale must have H_kv = {Hkv} elements, got {alpha.numel()}")
         with torch.cuda.device(k.device):
             _lib.check(L.cra_relay_build_shard(k.data_ptr(), v.data_ptr(), _lib.strides3(k), _lib.strides3(v), B, Hkv,
                                                seq_len, row_begin, rows, D, _dtype_code(k.dtype), int(use_relay),
@@ -174,7 +179,7 @@ def seq_parallel_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, seq_
         world = dist.get_world_size(group)
         rank = dist.get_rank(group)
     ops = ops or LibcraShardOps()
-    begin, end = seq_shard(seq_len, world, rank)
+    begin, end = seq_shard(seq_len, world, rank, relay_top_k)
     if q.shape[2] != end - begin or k.shape[2] != end - begin:
         raise ValueError(f"rank {rank} owns rows [{begin}, {end}) but got {q.shape[2]}")
     W = window(seq_len)
@@ -182,14 +187,14 @@ def seq_parallel_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, seq_
     R = 1 + relay_top_k if use_relay else 1
     # 1) global rows of this rank's blocks, then the whole list everywhere
     gk, gv = ops.relay_build_shard(k, v, seq_len, begin, use_relay, relay_top_k, relay_log_scale)
-    rows = [((e - b + W - 1) // W) * R for b, e in (seq_shard(seq_len, world, r) for r in range(world))]
+    rows = [((e - b + W - 1) // W) * R for b, e in (seq_shard(seq_len, world, r, relay_top_k) for r in range(world))]
     gk = _all_gather_padded(gk, 2, rows, group)
     gv = _all_gather_padded(gv, 2, rows, group)
     # 2) halo: the last W - 1 K/V rows of the previous rank
     halo = W - 1
     tail_k = k[:, :, max(0, k.shape[2] - halo):]
     tail_v = v[:, :, max(0, v.shape[2] - halo):]
-    sizes = [min(halo, e - b) for b, e in (seq_shard(seq_len, world, r) for r in range(world))]
+    sizes = [min(halo, e - b) for b, e in (seq_shard(seq_len, world, r, relay_top_k) for r in range(world))]
     hk = _all_gather_padded(tail_k, 2, sizes, group)
     hv = _all_gather_padded(tail_v, 2, sizes, group)
     if rank > 0:

@@ -598,9 +598,11 @@ __global__ void __launch_bounds__(320, 1) keyglobal_kernel(const __grid_constant
         bulk_load(ld + kUnit * 4, p.delta + li, kUnit * 4, BAR(C::B_QFULL + st));
         ++issued;
       }
-      if (*abort_flag)
+      if (*abort_flag) {
         for (int u = (issued > C::NSQ ? issued - C::NSQ : 0); u < issued; ++u)
           mbar_wait_bounded(BAR(C::B_QFULL + u % C::NSQ), (u / C::NSQ) & 1);
+        mbar_wait_bounded(BAR(C::B_KVFULL), 0);  // the K / V tile
+      }
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -1025,19 +1027,23 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
       }
     }
   } else {
-    // ---------------- epilogue: dK, dV (+ dG fold-in) -> global ----------------
+    // ---------------- epilogue: dK, dV -> global, then the dG fold-in ----------------
+    // The accumulators are read, scaled, rounded and stored first, and
+    // released as soon as the last TMEM load has landed: the next tile's
+    // first dV / dK product waits for that release, so nothing slow may sit
+    // between ACCFULL and ACCFREE.  The global-row gradients that belong to
+    // this key position (its strided row and relay rows whose source it is)
+    // are added afterwards by a read-add-write of the stored row in the
+    // output dtype -- the reference's relay scatter does the same
+    // (core.py:2811-2815) -- by the thread that stored it, so program order
+    // makes its own stores visible to the re-read.
     const int r = ((warp & 3) << 5) | lane;
     const uint32_t lane_off = static_cast<uint32_t>(r & ~31) << 16;
     for (int t = blockIdx.x, i = 0; t < n_tiles; t += gridDim.x, ++i) {
       const KeyLocalTile tl(t, p.n_ktiles, Hkv, S, W, groups);
-      PROF_T(te);
-      if (!mbar_wait(BAR(C::B_ACCFULL), i & 1, ab)) break;
-      PROF_ADD(16, te);
-      PROF_T(tb);
-      tc_fence_after();
       const int kj = tl.k0 + r;
       const bool row_ok = kj < S;
-      // global-row gradients that belong to this key position
+      // global rows of this key position (looked up before the wait)
       const int blk = kj / W;
       const int64_t gbase = (static_cast<int64_t>(tl.b) * Hkv + tl.hk) * static_cast<int64_t>(p.NG);
       int grow[5];
@@ -1061,53 +1067,67 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
             }
         }
       }
+      T* const dkrow = reinterpret_cast<T*>(p.dk) + tl.b * p.dk_sb + tl.hk * p.dk_sh + static_cast<int64_t>(kj) * p.dk_ss;
+      T* const dvrow = reinterpret_cast<T*>(p.dv) + tl.b * p.dv_sb + tl.hk * p.dv_sh + static_cast<int64_t>(kj) * p.dv_ss;
+      PROF_T(te);
+      if (!mbar_wait(BAR(C::B_ACCFULL), i & 1, ab)) break;
+      PROF_ADD(16, te);
+      PROF_T(tb);
+      tc_fence_after();
 #pragma unroll 1
-      for (int which = 0; which < 2; ++which) {  // 0: dK (scaled), 1: dV
-        const uint32_t acc = tmem + lane_off + (which == 0 ? C::COL_DK : C::COL_DV);
+      for (int g4 = 0; g4 < 2 * (D / 64); ++g4) {  // 64-column groups: dK then dV
+        const int which = g4 / (D / 64), c2 = g4 % (D / 64);
+        const uint32_t acc = tmem + lane_off + (which == 0 ? C::COL_DK : C::COL_DV) + 64 * c2;
         const float mul = which == 0 ? p.scale : 1.f;
-        const float* dg = which == 0 ? p.dgk : p.dgv;
-        T* drow = which == 0
-                      ? reinterpret_cast<T*>(p.dk) + tl.b * p.dk_sb + tl.hk * p.dk_sh + static_cast<int64_t>(kj) * p.dk_ss
-                      : reinterpret_cast<T*>(p.dv) + tl.b * p.dv_sb + tl.hk * p.dv_sh + static_cast<int64_t>(kj) * p.dv_ss;
-        // two 32-column TMEM loads per wait: half the round trips before the
-        // accumulators can be released
-#pragma unroll 1
-        for (int c2 = 0; c2 < D / 64; ++c2) {
-          float v[2][32];
-          tmem_ld32(acc + 64 * c2, v[0]);
-          tmem_ld32(acc + 64 * c2 + 32, v[1]);
-          tmem_ld_wait();
-          if (which == 1 && c2 == D / 64 - 1) {  // every TMEM read of this tile's dK / dV done
-            tc_fence_before();
-            mbar_arrive(BAR(C::B_ACCFREE));
-          }
-          if (row_ok) {
+        float v[2][32];
+        tmem_ld32(acc, v[0]);
+        tmem_ld32(acc + 32, v[1]);
+        tmem_ld_wait();
+        if (g4 == 2 * (D / 64) - 1) {  // every TMEM read of this tile's dK / dV done
+          tc_fence_before();
+          mbar_arrive(BAR(C::B_ACCFREE));
+        }
+        if (row_ok) {
+          T* drow = (which == 0 ? dkrow : dvrow) + 64 * c2;
 #pragma unroll
-            for (int h2 = 0; h2 < 2; ++h2) {
-              const int c = 2 * c2 + h2;
+          for (int h2 = 0; h2 < 2; ++h2)
 #pragma unroll
-              for (int e = 0; e < 32; ++e) v[h2][e] *= mul;
-              for (int gi = 0; gi < ng; ++gi) {
-                const float* gr = dg + (gbase + grow[gi]) * D + 32 * c;
-#pragma unroll
-                for (int e = 0; e < 32; e += 4) {
-                  const float4 a4 = *reinterpret_cast<const float4*>(gr + e);
-                  v[h2][e] += gsc[gi] * a4.x;
-                  v[h2][e + 1] += gsc[gi] * a4.y;
-                  v[h2][e + 2] += gsc[gi] * a4.z;
-                  v[h2][e + 3] += gsc[gi] * a4.w;
-                }
-              }
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                uint4 a4;
-                a4.x = E::pack(v[h2][8 * q + 0], v[h2][8 * q + 1]);
-                a4.y = E::pack(v[h2][8 * q + 2], v[h2][8 * q + 3]);
-                a4.z = E::pack(v[h2][8 * q + 4], v[h2][8 * q + 5]);
-                a4.w = E::pack(v[h2][8 * q + 6], v[h2][8 * q + 7]);
-                *reinterpret_cast<uint4*>(drow + 32 * c + 8 * q) = a4;
-              }
+            for (int q = 0; q < 4; ++q) {
+              uint4 a4;
+              a4.x = E::pack(v[h2][8 * q + 0] * mul, v[h2][8 * q + 1] * mul);
+              a4.y = E::pack(v[h2][8 * q + 2] * mul, v[h2][8 * q + 3] * mul);
+              a4.z = E::pack(v[h2][8 * q + 4] * mul, v[h2][8 * q + 5] * mul);
+              a4.w = E::pack(v[h2][8 * q + 6] * mul, v[h2][8 * q + 7] * mul);
+              *reinterpret_cast<uint4*>(drow + 32 * h2 + 8 * q) = a4;
             }
+        }
+      }
+      // fold-in: d{K,V}[kj] += sum_g gsc_g * dG_{k,v}[g], summed in fp32 onto the stored value
+      if (ng > 0) {
+#pragma unroll 1
+        for (int which = 0; which < 2; ++which) {
+          const float* dg = which == 0 ? p.dgk : p.dgv;
+          T* drow = which == 0 ? dkrow : dvrow;
+#pragma unroll 1
+          for (int c = 0; c < D; c += 8) {
+            const uint4 cur = *reinterpret_cast<const uint4*>(drow + c);
+            const uint32_t cw[4] = {cur.x, cur.y, cur.z, cur.w};
+            float a[8];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = E::unpack(cw[e]);
+              a[2 * e] = f.x;
+              a[2 * e + 1] = f.y;
+            }
+            for (int gi = 0; gi < ng; ++gi) {
+              const float* gr = dg + (gbase + grow[gi]) * D + c;
+              const float4 x0 = *reinterpret_cast<const float4*>(gr);
+              const float4 x1 = *reinterpret_cast<const float4*>(gr + 4);
+              a[0] += gsc[gi] * x0.x; a[1] += gsc[gi] * x0.y; a[2] += gsc[gi] * x0.z; a[3] += gsc[gi] * x0.w;
+              a[4] += gsc[gi] * x1.x; a[5] += gsc[gi] * x1.y; a[6] += gsc[gi] * x1.z; a[7] += gsc[gi] * x1.w;
+            }
+            *reinterpret_cast<uint4*>(drow + c) =
+                make_uint4(E::pack(a[0], a[1]), E::pack(a[2], a[3]), E::pack(a[4], a[5]), E::pack(a[6], a[7]));
           }
         }
       }
@@ -1191,15 +1211,33 @@ static cudaError_t set_smem(K kern, int bytes) {
   return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
+// Launch order of the backward kernels (dalpha_kernel only with a relay scale).
+static const char* const kBwdKernelNames[] = {"delta_kernel", "keyglobal_kernel", "reduce_kernel", "dalpha_kernel",
+                                              "keylocal_kernel", "dq_kernel"};
+
 template <int D, bool BF16>
-static cudaError_t launch_bwd_t(const BwdLaunch& L, cudaStream_t st) {
+static cudaError_t launch_bwd_t(const BwdLaunch& L_, cudaStream_t st) {
+  BwdLaunch& L = const_cast<BwdLaunch&>(L_);
   const QueryPassParams& qp = L.qp;
   const int B = qp.B, H = qp.H, S = qp.S;
   const int Spad = qp.n_qtiles * kTile;
   cudaError_t e;
+  int nk = 0;
+  L.n_kernels = 0;
+  // records the event before kernel `id` (index into kBwdKernelNames)
+  auto mark = [&](int id) -> cudaError_t {
+    if (!L.events) return cudaSuccess;
+    L.kernel_ids[nk] = id;
+    return cudaEventRecord(L.events[nk++], st);
+  };
+  auto done = [&]() -> cudaError_t {
+    L.n_kernels = nk;
+    return L.events ? cudaEventRecord(L.events[nk], st) : cudaSuccess;
+  };
   {
     constexpr int RPB = 8 * (32 / (D / 8));  // rows per 256-thread block
     dim3 grid((Spad + RPB - 1) / RPB, B * H);
+    if ((e = mark(0)) != cudaSuccess) return e;
     delta_kernel<D, BF16><<<grid, 256, 0, st>>>(L.o, L.d_o, L.o_st[0], L.o_st[1], L.o_st[2], L.do_st[0], L.do_st[1],
                                                 L.do_st[2], L.lse_in, H, S, Spad, L.lse2, L.delta);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
@@ -1210,18 +1248,21 @@ static cudaError_t launch_bwd_t(const BwdLaunch& L, cudaStream_t st) {
   {
     auto kern = keyglobal_kernel<D, BF16>;
     if ((e = set_smem(kern, KeyCfg<D>::SMEM)) != cudaSuccess) return e;
+    if ((e = mark(1)) != cudaSuccess) return e;
     kern<<<dim3(n_gtiles * gp.n_split, Hkv, B), 320, KeyCfg<D>::SMEM, st>>>(gp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   {
     const int64_t n4 = static_cast<int64_t>(B) * Hkv * gp.NG * D / 4;
     const int64_t nb = (n4 + 255) / 256;
+    if ((e = mark(2)) != cudaSuccess) return e;
     reduce_kernel<<<static_cast<int>(nb < 4096 ? nb : 4096), 256, 0, st>>>(
         reinterpret_cast<const float4*>(gp.part_k), reinterpret_cast<const float4*>(gp.part_v), n4, gp.n_split,
         reinterpret_cast<float4*>(L.dgk), reinterpret_cast<float4*>(L.dgv));
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   if (L.d_alpha && gp.R > 1) {
+    if ((e = mark(3)) != cudaSuccess) return e;
     dalpha_kernel<BF16><<<Hkv, 256, 0, st>>>(L.dgk, L.dgv, L.gk_rows, L.gv_rows, B, Hkv, gp.NG, gp.R, D, L.d_alpha);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
@@ -1230,6 +1271,7 @@ static cudaError_t launch_bwd_t(const BwdLaunch& L, cudaStream_t st) {
     auto kern = keylocal_kernel<D, BF16>;
     if ((e = set_smem(kern, KeyLocalCfg<D>::SMEM)) != cudaSuccess) return e;
     const int n_tiles = lp.n_ktiles * Hkv * B;
+    if ((e = mark(4)) != cudaSuccess) return e;
     kern<<<dim3(n_tiles < sm_count() ? n_tiles : sm_count()), KeyLocalCfg<D>::THREADS, KeyLocalCfg<D>::SMEM, st>>>(
         lp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
@@ -1238,10 +1280,16 @@ static cudaError_t launch_bwd_t(const BwdLaunch& L, cudaStream_t st) {
     auto kern = dq_kernel<D, BF16>;
     if ((e = set_smem(kern, DqCfg<D>::SMEM)) != cudaSuccess) return e;
     const int n_tiles = qp.n_qtiles * H * B;
+    if ((e = mark(5)) != cudaSuccess) return e;
     kern<<<dim3(n_tiles < sm_count() ? n_tiles : sm_count()), DqCfg<D>::THREADS, DqCfg<D>::SMEM, st>>>(qp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
-  return cudaSuccess;
+  return done();
+}
+
+const char* bwd_kernel_name(int id) {
+  return id >= 0 && id < static_cast<int>(sizeof(kBwdKernelNames) / sizeof(kBwdKernelNames[0])) ? kBwdKernelNames[id]
+                                                                                                : "unknown";
 }
 
 cudaError_t launch_bwd(const BwdLaunch& L, int D, bool bf16, cudaStream_t stream) {

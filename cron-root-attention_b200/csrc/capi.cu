@@ -175,6 +175,12 @@ BwdLayout bwd_layout(int batch, int heads, int kv_heads, int seq_len, int head_d
 
 }  // namespace
 
+namespace cra {
+// Records the detail text returned by cra_last_error_message for the calling
+// thread (used by the other C-ABI translation units).
+int set_last_error(int status, const char* text) { return fail(status, "%s", text); }
+}  // namespace cra
+
 extern "C" {
 
 const char* cra_status_string(int status) {
@@ -287,13 +293,20 @@ size_t cra_bwd_workspace_bytes(int batch, int heads, int kv_heads, int seq_len, 
   return bwd_layout(batch, heads, kv_heads, seq_len, head_dim, use_relay, top_k).total;
 }
 
-int cra_bwd(const void* q, const void* k, const void* v, const void* o, const void* d_o, const float* lse,
-            const void* g_k, const void* g_v, const int32_t* g_src, const int64_t* q_strides,
-            const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides, const int64_t* do_strides,
-            int batch, int heads, int kv_heads, int seq_len, int head_dim, int dtype, int use_relay, int top_k,
-            float softmax_scale, const float* relay_log_scale, void* dq, void* dk, void* dv,
-            const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
-            float* d_relay_log_scale, void* workspace, size_t workspace_bytes, int* dev_error, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// cra_bwd's body; with `events` non-null (BwdLaunch::kMaxKernels + 1 of
+// them) an event is recorded before each kernel and after the last.
+int bwd_impl(const void* q, const void* k, const void* v, const void* o, const void* d_o, const float* lse,
+             const void* g_k, const void* g_v, const int32_t* g_src, const int64_t* q_strides,
+             const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides, const int64_t* do_strides,
+             int batch, int heads, int kv_heads, int seq_len, int head_dim, int dtype, int use_relay, int top_k,
+             float softmax_scale, const float* relay_log_scale, void* dq, void* dk, void* dv,
+             const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
+             float* d_relay_log_scale, void* workspace, size_t workspace_bytes, int* dev_error, void* stream,
+             cudaEvent_t* events, int* n_kernels, int* kernel_ids) {
   CRA_TRY(check_common(batch, heads, kv_heads, seq_len, head_dim, dtype, top_k));
   CRA_TRY(check_tensor("q", q, q_strides, batch, heads));
   CRA_TRY(check_tensor("k", k, k_strides, batch, kv_heads));
@@ -416,8 +429,67 @@ int cra_bwd(const void* q, const void* k, const void* v, const void* o, const vo
     const cudaError_t me = cudaMemsetAsync(d_relay_log_scale, 0, sizeof(float) * kv_heads, st);
     if (me != cudaSuccess) return fail(CRA_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(me));
   }
+  L.events = events;
   cudaError_t e = launch_bwd(L, head_dim, bf16, st);
+  if (n_kernels) *n_kernels = L.n_kernels;
+  if (kernel_ids)
+    for (int i = 0; i < L.n_kernels; ++i) kernel_ids[i] = L.kernel_ids[i];
   return e == cudaSuccess ? CRA_OK : fail(CRA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+}
+
+}  // namespace
+
+extern "C" {
+
+int cra_bwd(const void* q, const void* k, const void* v, const void* o, const void* d_o, const float* lse,
+            const void* g_k, const void* g_v, const int32_t* g_src, const int64_t* q_strides,
+            const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides, const int64_t* do_strides,
+            int batch, int heads, int kv_heads, int seq_len, int head_dim, int dtype, int use_relay, int top_k,
+            float softmax_scale, const float* relay_log_scale, void* dq, void* dk, void* dv,
+            const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
+            float* d_relay_log_scale, void* workspace, size_t workspace_bytes, int* dev_error, void* stream) {
+  return bwd_impl(q, k, v, o, d_o, lse, g_k, g_v, g_src, q_strides, k_strides, v_strides, o_strides, do_strides,
+                  batch, heads, kv_heads, seq_len, head_dim, dtype, use_relay, top_k, softmax_scale, relay_log_scale,
+                  dq, dk, dv, dq_strides, dk_strides, dv_strides, d_relay_log_scale, workspace, workspace_bytes,
+                  dev_error, stream, nullptr, nullptr, nullptr);
+}
+
+int cra_bwd_kernel_times(const void* q, const void* k, const void* v, const void* o, const void* d_o,
+                         const float* lse, const void* g_k, const void* g_v, const int32_t* g_src,
+                         const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                         const int64_t* o_strides, const int64_t* do_strides, int batch, int heads, int kv_heads,
+                         int seq_len, int head_dim, int dtype, int use_relay, int top_k, float softmax_scale,
+                         const float* relay_log_scale, void* dq, void* dk, void* dv, const int64_t* dq_strides,
+                         const int64_t* dk_strides, const int64_t* dv_strides, float* d_relay_log_scale,
+                         void* workspace, size_t workspace_bytes, int* dev_error, void* stream, float* kernel_ms,
+                         const char** kernel_names, int max_kernels, int* n_kernels) {
+  if (!kernel_ms || !n_kernels) return fail(CRA_ERR_INVALID_ARGUMENT, "kernel_ms / n_kernels: null pointer");
+  CRA_TRY(bind_context());
+  cudaEvent_t ev[BwdLaunch::kMaxKernels + 1];
+  int made = 0;
+  cudaError_t e = cudaSuccess;
+  for (; made <= BwdLaunch::kMaxKernels && e == cudaSuccess; ++made) e = cudaEventCreate(&ev[made]);
+  if (e != cudaSuccess) made -= 1;
+  int status = e == cudaSuccess ? CRA_OK : fail(CRA_ERR_CUDA, "cudaEventCreate: %s", cudaGetErrorString(e));
+  int n = 0;
+  int ids[BwdLaunch::kMaxKernels] = {};
+  if (status == CRA_OK)
+    status = bwd_impl(q, k, v, o, d_o, lse, g_k, g_v, g_src, q_strides, k_strides, v_strides, o_strides, do_strides,
+                      batch, heads, kv_heads, seq_len, head_dim, dtype, use_relay, top_k, softmax_scale,
+                      relay_log_scale, dq, dk, dv, dq_strides, dk_strides, dv_strides, d_relay_log_scale, workspace,
+                      workspace_bytes, dev_error, stream, ev, &n, ids);
+  if (status == CRA_OK) {
+    e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) status = fail(CRA_ERR_CUDA, "cudaStreamSynchronize: %s", cudaGetErrorString(e));
+  }
+  for (int i = 0; status == CRA_OK && i < n && i < max_kernels; ++i) {
+    e = cudaEventElapsedTime(&kernel_ms[i], ev[i], ev[i + 1]);
+    if (e != cudaSuccess) status = fail(CRA_ERR_CUDA, "cudaEventElapsedTime: %s", cudaGetErrorString(e));
+    if (kernel_names) kernel_names[i] = bwd_kernel_name(ids[i]);
+  }
+  *n_kernels = status == CRA_OK ? (n < max_kernels ? n : max_kernels) : 0;
+  for (int i = 0; i < made; ++i) cudaEventDestroy(ev[i]);
+  return status;
 }
 
 int cra_relay_build_shard(const void* k, const void* v, const int64_t* k_strides, const int64_t* v_strides,

@@ -155,9 +155,11 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
       }
       // Do not leave while copies into this CTA's shared memory are in
       // flight (only reachable after an abort).
-      if (*abort_flag)
+      if (*abort_flag) {
         for (int i = (issued > C::NSLOT ? issued - C::NSLOT : 0); i < issued; ++i)
           mbar_wait_bounded(BAR(C::B_FULL + i % C::NSLOT), (i / C::NSLOT) & 1);
+        mbar_wait_bounded(BAR(C::B_QFULL), 0);  // the Q tiles
+      }
     }
     __syncwarp();
   } else if (warp == 1) {

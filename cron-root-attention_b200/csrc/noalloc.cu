@@ -4,9 +4,11 @@
 // the contract (size limit, first-call set-up, no overlapping calls).
 #include <cuda_runtime.h>
 
+#include <cstdio>
 #include <mutex>
 
 #include "../../include/cra.h"
+#include "params.h"
 
 namespace {
 
@@ -23,13 +25,15 @@ void* g_scratch_ptr[kMaxDevices] = {};
 int scratch_address(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return CRA_ERR_CUDA;
-  if (dev < 0 || dev >= kMaxDevices) return CRA_ERR_UNSUPPORTED;
+  if (e != cudaSuccess) return cra::set_last_error(CRA_ERR_CUDA, "cra_bwd_noalloc: cudaGetDevice failed");
+  if (dev < 0 || dev >= kMaxDevices)
+    return cra::set_last_error(CRA_ERR_UNSUPPORTED, "cra_bwd_noalloc: device index beyond 63");
   std::lock_guard<std::mutex> lock(g_mu);
   if (!g_scratch_ptr[dev]) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_bwd_scratch);
-    if (e != cudaSuccess || !p) return CRA_ERR_CUDA;
+    if (e != cudaSuccess || !p)
+      return cra::set_last_error(CRA_ERR_CUDA, "cra_bwd_noalloc: cudaGetSymbolAddress of the scratch array failed");
     g_scratch_ptr[dev] = p;
   }
   *out = g_scratch_ptr[dev];
@@ -47,7 +51,12 @@ extern "C" int cra_bwd_noalloc(const void* q, const void* k, const void* v, cons
                                const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
                                float* d_relay_log_scale, int* dev_error, void* stream) {
   const size_t need = cra_bwd_workspace_bytes(batch, heads, kv_heads, seq_len, head_dim, use_relay, top_k);
-  if (need > CRA_BWD_NOALLOC_SCRATCH_BYTES) return CRA_ERR_WORKSPACE;  // too large for the fixed scratch
+  if (need > CRA_BWD_NOALLOC_SCRATCH_BYTES) {  // too large for the fixed scratch
+    char text[160];
+    snprintf(text, sizeof(text), "cra_bwd_noalloc: these sizes need %zu bytes of scratch > %u (the fixed maximum)",
+             need, static_cast<unsigned>(CRA_BWD_NOALLOC_SCRATCH_BYTES));
+    return cra::set_last_error(CRA_ERR_WORKSPACE, text);
+  }
   void* scratch = nullptr;
   const int s = scratch_address(&scratch);
   if (s != CRA_OK) return s;

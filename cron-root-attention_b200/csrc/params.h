@@ -70,8 +70,20 @@ struct BwdLaunch {
   float* d_alpha;          // [Hkv] or null
   const void* gk_rows;     // G_k / G_v (for d_alpha)
   const void* gv_rows;
+  // Optional timing: when non-null, events[i] is recorded on the stream just
+  // before kernel i and events[n_kernels] after the last one.
+  static constexpr int kMaxKernels = 8;
+  cudaEvent_t* events;
+  int n_kernels;                // set by launch_bwd: kernels launched (timed)
+  int kernel_ids[kMaxKernels];  // set by launch_bwd: which kernel each was
 };
 
+// Name of the backward kernel with id `id` (BwdLaunch::kernel_ids).
+const char* bwd_kernel_name(int i);
+
 cudaError_t launch_bwd(const BwdLaunch& L, int D, bool bf16, cudaStream_t stream);
+
+// Sets the calling thread's cra_last_error_message text; returns status.
+int set_last_error(int status, const char* text);
 
 }  // namespace cra

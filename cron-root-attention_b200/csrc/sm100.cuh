@@ -35,6 +35,12 @@ enum DeviceError : int {
 #ifndef CRA_WAIT_LIMIT_NS
 #define CRA_WAIT_LIMIT_NS 500000000ull  // 0.5 s: far above any legitimate wait
 #endif
+// Limit of the drain waits on abort paths (copies and MMAs already in flight
+// always complete; this only bounds the spin).  Kept separate so that a build
+// with a tiny CRA_WAIT_LIMIT_NS still lets in-flight work land.
+#ifndef CRA_DRAIN_LIMIT_NS
+#define CRA_DRAIN_LIMIT_NS 500000000ull
+#endif
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -265,7 +271,7 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 // Bounded spin used only on abort paths (no abort flag to consult).
 __device__ __forceinline__ void mbar_wait_bounded(uint32_t bar, uint32_t parity) {
   const uint64_t t0 = globaltimer();
-  while (!mbar_try(bar, parity) && globaltimer() - t0 < CRA_WAIT_LIMIT_NS) {
+  while (!mbar_try(bar, parity) && globaltimer() - t0 < CRA_DRAIN_LIMIT_NS) {
   }
 }
 

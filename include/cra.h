@@ -145,6 +145,22 @@ int cra_bwd(const void* q, const void* k, const void* v, const void* o, const vo
             const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
             float* d_relay_log_scale, void* workspace, size_t workspace_bytes, int* dev_error, void* stream);
 
+/* Measurement helper (no counterpart in the reference): runs cra_bwd with the
+ * same arguments, records a CUDA event on `stream` before each of its kernels
+ * and after the last, SYNCHRONIZES the stream, and returns each kernel's
+ * event-to-event time in kernel_ms[i] (ms) and its name in kernel_names[i]
+ * (static strings; may be NULL) for i < *n_kernels <= max_kernels, in launch
+ * order.  For benchmarks and profiles only. */
+int cra_bwd_kernel_times(const void* q, const void* k, const void* v, const void* o, const void* d_o,
+                         const float* lse, const void* g_k, const void* g_v, const int32_t* g_src,
+                         const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                         const int64_t* o_strides, const int64_t* do_strides, int batch, int heads, int kv_heads,
+                         int seq_len, int head_dim, int dtype, int use_relay, int top_k, float softmax_scale,
+                         const float* relay_log_scale, void* dq, void* dk, void* dv, const int64_t* dq_strides,
+                         const int64_t* dk_strides, const int64_t* dv_strides, float* d_relay_log_scale,
+                         void* workspace, size_t workspace_bytes, int* dev_error, void* stream, float* kernel_ms,
+                         const char** kernel_names, int max_kernels, int* n_kernels);
+
 /* Backward without a caller-provided workspace, for callers that cannot
  * allocate device memory (no access to an allocator, or code that must not
  * allocate at all, such as a plug-in running under a host framework that owns
@@ -154,7 +170,9 @@ int cra_bwd(const void* q, const void* k, const void* v, const void* o, const vo
  * (32 MiB) on every GPU that loads the library, held until the process exits.
  * Sizes whose cra_bwd_workspace_bytes() exceeds that return
  * CRA_ERR_WORKSPACE.  The first call on a device looks up the array's device
- * address (cudaGetSymbolAddress, with that device current); make that first
+ * address (cudaGetSymbolAddress, with that device current) and keeps it for
+ * the rest of the process: the address belongs to the CUDA context current at
+ * that first call, so it is stale after cudaDeviceReset.  Make that first
  * call before any stream capture.  Calls share the array: two calls whose
  * work overlaps on the GPU (different streams, or different host threads
  * without ordering) race and corrupt each other's results.  Nothing in the

@@ -91,3 +91,11 @@ def test_validation_errors_without_gpu(L):
     r = L.cra_bwd(p, p, p, p, p, p, p, p, p, st, st, st, st, st, 1, 2, 2, 300, 64, 0, 0, 2, ctypes.c_float(0.125),
                   None, p, p, p, st, st, st, None, p, ws - 1, None, None)
     assert r == 4 and b"workspace" in L.cra_last_error_message()
+
+
+def test_wait_probe_library_loads():
+    """The test-only bounded-wait probe library is built beside libcra and
+    exports its one entry point (run on the GPU by test_wait_timeout_gpu)."""
+    from test_wait_timeout_gpu import PROBE
+    h = ctypes.CDLL(PROBE)
+    assert hasattr(h, "cra_test_wait_timeout")

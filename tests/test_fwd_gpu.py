@@ -85,6 +85,31 @@ def test_config2_full_size(cuda_device):
     assert r["ok"], r
 
 
+def _device_inputs(B, H, S, D, dt, seed, sigma, dev):
+    """Seeded inputs drawn on the device (q, k, v in that order, N(0,1) * sigma,
+    cast to dt): the BASELINE shapes at full size are too large to draw on the
+    host in reasonable time."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    return tuple((torch.randn(B, H, S, D, generator=g, device=dev) * sigma).to(dt) for _ in range(3))
+
+
+def test_config4_full_size(cuda_device):
+    """BASELINE config 4 at full size on one GPU: B1 H32 D128 S262144 fp16,
+    N(0,1) * 0.5, seed 3 (device generator).  Two whole heads checked row by
+    row against the oracle."""
+    dev = cuda_device
+    q, k, v = _device_inputs(1, 32, 262144, 128, torch.float16, 3, 0.5, dev)
+    o = _cra().cron_root_attention(q, k, v)
+    torch.cuda.synchronize(dev)
+    assert _cra().check_device_errors(dev) == 0
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    for h in (0, 21):
+        sl = lambda t: t[:, h:h + 1].cpu()
+        ref, _ = O.forward(sl(q), sl(k), sl(v))
+        r = fwd_check(sl(o), ref, torch.float16, v_rms=0.5)
+        assert r["ok"], (h, r)
+
+
 @pytest.mark.parametrize("top_k", [1, 3, 4])
 def test_relay_top_k(top_k, cuda_device):
     q, k, v = inputs(1, 2, 2, 2600, 64, torch.float16, 20 + top_k)

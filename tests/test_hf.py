@@ -129,3 +129,28 @@ def test_llama_forward_backward_on_gpu_matches_oracle(cuda_device):
                        relay_dtype=torch.bfloat16)
     res = fwd_check(o.transpose(1, 2), ref, torch.bfloat16, v_rms=v.float().pow(2).mean().sqrt().item())
     assert res["ok"], res
+
+
+def test_causal_only_masks_are_accepted(recorder):
+    m = torch.nn.Module()
+    q = torch.randn(2, 2, 8, 64)
+    tril = torch.ones(8, 8, dtype=torch.bool).tril()
+    additive = torch.zeros(2, 1, 8, 8).masked_fill(~tril, torch.finfo(torch.float32).min)
+    for mask in (None, tril.expand(2, 1, 8, 8), additive, torch.ones(2, 8, dtype=torch.long)):
+        hf.cron_root_attention_forward(m, q, q, q, mask)
+    assert len(recorder) == 4
+
+
+def test_padding_masks_raise(recorder):
+    m = torch.nn.Module()
+    q = torch.randn(2, 2, 8, 64)
+    pad = torch.ones(2, 8, dtype=torch.long)
+    pad[1, :3] = 0  # left padding of the second sequence
+    tril = torch.ones(8, 8, dtype=torch.bool).tril()
+    keep4d = tril.expand(2, 1, 8, 8).clone()
+    keep4d[1, :, :, :3] = False
+    additive = torch.zeros(2, 1, 8, 8).masked_fill(~keep4d, torch.finfo(torch.float32).min)
+    for mask in (pad, keep4d, additive):
+        with pytest.raises(NotImplementedError, match="mask"):
+            hf.cron_root_attention_forward(m, q, q, q, mask)
+    assert recorder == []

@@ -20,22 +20,23 @@ def test_shard_units_partition(B, H, world):
     assert sorted(seen) == [(b, h) for b in range(B) for h in range(H)]
 
 
-@pytest.mark.parametrize("S,world", [(524288, 8), (65536, 2), (3000, 3), (2049, 2)])
-def test_seq_shard_block_aligned_cover(S, world):
+@pytest.mark.parametrize("S,world,top_k", [(524288, 8, 2), (65536, 2, 2), (3000, 3, 2), (2049, 2, 2),
+                                           (65536, 4, 4), (40000, 8, 1)])
+def test_seq_shard_block_aligned_cover(S, world, top_k):
     W = window(S)
     prev = 0
     for r in range(world):
-        b, e = seq_shard(S, world, r)
+        b, e = seq_shard(S, world, r, top_k)
         assert b == prev and b % W == 0 and e > b
         prev = e
     assert prev == S
     # about equal attention work per rank: visible keys per query counted
     # independently (local window + strided and relay rows of earlier blocks)
-    R = 3 if S > 2048 else 1
+    R = 1 + top_k if S > 2048 else 1
     def keys(m):
         ls = max(m - W + 1, 0)
         return min(m + 1, W) + R * (ls // W) + (ls % W != 0)
-    work = [sum(keys(m) for m in range(*seq_shard(S, world, r))) for r in range(world)]
+    work = [sum(keys(m) for m in range(*seq_shard(S, world, r, top_k))) for r in range(world)]
     block = max(sum(keys(m) for m in range(b, min(b + W, S))) for b in range(0, S, W))
     assert max(work) - sum(work) / world <= block
     if S == 524288:
@@ -96,3 +97,12 @@ def test_seq_parallel_forward_without_process_group(S):
     o = seq_parallel_forward(q, k, v, S, ops=OracleShardOps())
     ref, _ = O.forward(q, k, v, dtype=torch.float64)
     assert (o - ref).abs().max().item() < 1e-10
+
+
+def test_relay_build_shard_rejects_wrong_scale_length():
+    """A relay scale with the wrong number of kv heads is refused on the host,
+    before anything reaches a kernel."""
+    from cron_root_attention.parallel import LibcraShardOps
+    k = torch.zeros(1, 2, 3000, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="relay_log_scale"):
+        LibcraShardOps().relay_build_shard(k, k, 3000, 0, True, 2, torch.zeros(3))

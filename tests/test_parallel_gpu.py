@@ -45,6 +45,28 @@ def test_sequence_split_emulated_on_one_gpu(S, world, D, dt, cuda_device):
     assert r["ok"], r
 
 
+def test_config5_shape_split_eight_ways(cuda_device):
+    """BASELINE config 5's exact shape -- S = 524288 (W = 725, not a perfect
+    square), D128 bf16, N(0,1), seed 4 (device generator) -- for two of its 16
+    heads, split 8 ways as the 8-GPU run splits it, every shard run on this
+    GPU, whole output checked row by row against the oracle."""
+    dev = cuda_device
+    S, H = 524288, 16
+    g = torch.Generator(device=dev).manual_seed(4)
+    q, k, v = (torch.randn(1, H, S, 128, generator=g, device=dev).to(torch.bfloat16) for _ in range(3))
+    heads = [0, 9]
+    q, k, v = (t[:, heads].contiguous() for t in (q, k, v))
+    from cron_root_attention.parallel import window
+    assert window(S) == 725
+    o = _emulate(q, k, v, S, 8, dev)
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    for i in range(len(heads)):
+        sl = lambda t: t[:, i:i + 1].cpu()
+        ref, _ = O.forward(sl(q), sl(k), sl(v))
+        r = fwd_check(sl(o), ref, torch.bfloat16)
+        assert r["ok"], (heads[i], r)
+
+
 def _port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
