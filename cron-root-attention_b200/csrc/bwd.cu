@@ -31,13 +31,63 @@
 #include "params.h"
 #include "sm100.cuh"
 
+#include <type_traits>
+
 namespace cra {
 
 constexpr float kLog2e = 1.4426950408889634f;
 
+// Bit e set iff column e of a 32-column chunk lies in [lo, hi) (bounds
+// relative to the chunk's first column, any range).
+__device__ __forceinline__ uint32_t col_mask32(int lo, int hi) {
+  const int a = min(max(lo, 0), 32), z = min(max(hi, 0), 32);
+  const uint32_t mz = z >= 32 ? 0xffffffffu : ((1u << z) - 1u);
+  const uint32_t ma = a >= 32 ? 0xffffffffu : ((1u << a) - 1u);
+  return mz & ~ma;
+}
+
+// Key-centric softmax of one 32-column chunk (columns = queries): P^T =
+// 2^(s scale log2e + nlse) and dS^T = P^T (dP^T + ndelta), with the per-query
+// nlse = -lse log2e and ndelta = -Di read four at a time from shared memory
+// (warp-wide broadcasts) and the arithmetic done two columns per f32x2
+// instruction.  Columns outside `m` give 0; a warp whose chunk is entirely
+// visible skips the selects.
+template <typename E>
+__device__ __forceinline__ void key_softmax_chunk(const float (&s)[32], const float (&dp)[32],
+                                                  const float* __restrict__ nlse, const float* __restrict__ ndi,
+                                                  float sl2, uint32_t m, uint32_t (&ppk)[16], uint32_t (&dpk)[16]) {
+  const float2 sl2x2 = make_float2(sl2, sl2);
+  auto body = [&](auto masked) {
+#pragma unroll
+    for (int e4 = 0; e4 < 8; ++e4) {
+      const float4 l = reinterpret_cast<const float4*>(nlse)[e4];
+      const float4 d = reinterpret_cast<const float4*>(ndi)[e4];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int e = 4 * e4 + 2 * h;
+        const float2 x = fma2(make_float2(s[e], s[e + 1]), sl2x2, h ? make_float2(l.z, l.w) : make_float2(l.x, l.y));
+        float p0 = ex2(x.x), p1 = ex2(x.y);
+        if constexpr (decltype(masked)::value) {
+          p0 = (m >> e) & 1u ? p0 : 0.f;
+          p1 = (m >> (e + 1)) & 1u ? p1 : 0.f;
+        }
+        const float2 ds = mul2(make_float2(p0, p1),
+                               add2(make_float2(dp[e], dp[e + 1]), h ? make_float2(d.z, d.w) : make_float2(d.x, d.y)));
+        ppk[e / 2] = E::pack(p0, p1);
+        dpk[e / 2] = E::pack(ds.x, ds.y);
+      }
+    }
+  };
+  if (__all_sync(0xffffffffu, m == 0xffffffffu))
+    body(std::false_type{});
+  else
+    body(std::true_type{});
+}
+
 // ===========================================================================
-// delta: Di = rowsum(O * dO);  lse2 = lse * log2(e).  Rows >= S of the padded
-// arrays are zero (never read unmasked).
+// delta: ndelta = -rowsum(O * dO);  nlse2 = -lse * log2(e).  Both are stored
+// negated so the softmax passes add them with one packed f32x2 instruction
+// per two columns.  Rows >= S of the padded arrays are zero (always masked).
 // ===========================================================================
 template <int D, bool BF16>
 __global__ void __launch_bounds__(256) delta_kernel(const void* __restrict__ op, const void* __restrict__ dop,
@@ -71,8 +121,8 @@ __global__ void __launch_bounds__(256) delta_kernel(const void* __restrict__ op,
   for (int off = LPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
   if (part == 0 && row < Spad) {
     const int64_t i = static_cast<int64_t>(bh) * Spad + row;
-    delta[i] = row < S ? acc : 0.f;
-    lse2[i] = row < S ? lse[static_cast<int64_t>(bh) * S + row] * kLog2e : 0.f;
+    delta[i] = row < S ? -acc : 0.f;
+    lse2[i] = row < S ? -lse[static_cast<int64_t>(bh) * S + row] * kLog2e : 0.f;
   }
 }
 
@@ -373,8 +423,9 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
       const int ls = local_start(qi, W);
       const int cnt = gcount(qi, W, R);
       const int64_t rowi = (static_cast<int64_t>(tl.b) * p.H + tl.h) * Spad + qi;
-      const float lse2 = p.lse[rowi];  // lse * log2(e), padded array
-      const float di = p.delta[rowi];
+      const float nl = p.lse[rowi];    // -lse * log2(e), padded array
+      const float nd = p.delta[rowi];  // -Di
+      const float2 sl2x2 = make_float2(sl2, sl2), nlx2 = make_float2(nl, nl), ndx2 = make_float2(nd, nd);
       for (int j = 0; ok && j < un.ntiles; ++j)
         for (int hh = 0; hh < 2; ++hh) {
           int row0;
@@ -405,14 +456,26 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
             tmem_ld32(scol + 32 * c, s);
             tmem_ld32(scol + 64 + 32 * c, dp);
             tmem_ld_wait();
+            const uint32_t m = col_mask32(lo - 32 * c, hi - 32 * c);
             uint32_t pk[16];
+            // dS = P (dP - Di), P = 2^(s scale log2e - lse log2e); masked columns 0
+            auto body = [&](auto masked) {
 #pragma unroll
-            for (int e2 = 0; e2 < 32; e2 += 2) {
-              const int col = 32 * c + e2;
-              const float p0 = (col >= lo && col < hi) ? ex2(fmaf(s[e2], sl2, -lse2)) : 0.f;
-              const float p1 = (col + 1 >= lo && col + 1 < hi) ? ex2(fmaf(s[e2 + 1], sl2, -lse2)) : 0.f;
-              pk[e2 / 2] = E::pack(p0 * (dp[e2] - di), p1 * (dp[e2 + 1] - di));
-            }
+              for (int e2 = 0; e2 < 32; e2 += 2) {
+                const float2 x = fma2(make_float2(s[e2], s[e2 + 1]), sl2x2, nlx2);
+                float p0 = ex2(x.x), p1 = ex2(x.y);
+                if constexpr (decltype(masked)::value) {
+                  p0 = (m >> e2) & 1u ? p0 : 0.f;
+                  p1 = (m >> (e2 + 1)) & 1u ? p1 : 0.f;
+                }
+                const float2 ds = mul2(make_float2(p0, p1), add2(make_float2(dp[e2], dp[e2 + 1]), ndx2));
+                pk[e2 / 2] = E::pack(ds.x, ds.y);
+              }
+            };
+            if (__all_sync(0xffffffffu, m == 0xffffffffu))
+              body(std::false_type{});
+            else
+              body(std::true_type{});
             tmem_st16(scol + 16 * c, pk);  // dS over S columns [16c, 16c+16), already read
           }
           tmem_st_wait();
@@ -448,8 +511,12 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
         typename E::T* orow = reinterpret_cast<typename E::T*>(p.out) + tl.b * p.out_sb + tl.h * p.out_sh +
                               static_cast<int64_t>(qi) * p.out_ss;
 #pragma unroll
-        for (int q = 0; q < D / 8; ++q)
-          *reinterpret_cast<uint4*>(orow + 8 * q) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+        for (int q = 0; q < D / 16; ++q) {  // 16 columns = one 32-byte sector per store
+          uint32_t w8[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) w8[e] = pk[8 * q + e];
+          st_global_8w(orow + 16 * q, w8, p.out_v8);
+        }
       }
     }
   }
@@ -692,14 +759,8 @@ __global__ void __launch_bounds__(320, 1) keyglobal_kernel(const __grid_constant
         tmem_ld32(scol + 64 + 32 * c, dp);
         tmem_ld_wait();
         uint32_t ppk[16], dpk[16];
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const int col = 32 * c + e;
-          const float p0 = (col >= lo && col < hi) ? ex2(fmaf(s[e], sl2, -sm_lse[col])) : 0.f;
-          const float p1 = (col + 1 >= lo && col + 1 < hi) ? ex2(fmaf(s[e + 1], sl2, -sm_lse[col + 1])) : 0.f;
-          ppk[e / 2] = E::pack(p0, p1);
-          dpk[e / 2] = E::pack(p0 * (dp[e] - sm_di[col]), p1 * (dp[e + 1] - sm_di[col + 1]));
-        }
+        key_softmax_chunk<E>(s, dp, sm_lse + 32 * c, sm_di + 32 * c, sl2, col_mask32(lo - 32 * c, hi - 32 * c), ppk,
+                             dpk);
         // chunk c of P^T / dS^T overwrites score columns [16c, 16c+16) of
         // S^T / dP^T, already consumed (columns [0, 32c+32) have been read)
         tmem_st16(scol + 16 * c, ppk);
@@ -1002,19 +1063,9 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
           tmem_ld32(scol + 32 * c, s);
           tmem_ld32(scol + 64 + 32 * c, dp);
           tmem_ld_wait();
-          const int a = min(max(lo - 32 * c, 0), 32), z = min(max(hi - 32 * c, 0), 32);
-          const uint32_t mz = z >= 32 ? 0xffffffffu : ((1u << z) - 1u);
-          const uint32_t ma = a >= 32 ? 0xffffffffu : ((1u << a) - 1u);
-          const uint32_t m = mz & ~ma;
           uint32_t ppk[16], dpk[16];
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const int col = 32 * c + e;
-            const float p0 = (m & (1u << e)) ? ex2(fmaf(s[e], sl2, -sm_lse[col])) : 0.f;
-            const float p1 = (m & (2u << e)) ? ex2(fmaf(s[e + 1], sl2, -sm_lse[col + 1])) : 0.f;
-            ppk[e / 2] = E::pack(p0, p1);
-            dpk[e / 2] = E::pack(p0 * (dp[e] - sm_di[col]), p1 * (dp[e + 1] - sm_di[col + 1]));
-          }
+          key_softmax_chunk<E>(s, dp, sm_lse + 32 * c, sm_di + 32 * c, sl2, col_mask32(lo - 32 * c, hi - 32 * c),
+                               ppk, dpk);
           // chunk c of P^T / dS^T overwrites score columns [16c, 16c+16) of
           // S^T / dP^T, already consumed (columns [0, 32c+32) have been read)
           tmem_st16(scol + 16 * c, ppk);
@@ -1092,43 +1143,68 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
 #pragma unroll
           for (int h2 = 0; h2 < 2; ++h2)
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint4 a4;
-              a4.x = E::pack(v[h2][8 * q + 0] * mul, v[h2][8 * q + 1] * mul);
-              a4.y = E::pack(v[h2][8 * q + 2] * mul, v[h2][8 * q + 3] * mul);
-              a4.z = E::pack(v[h2][8 * q + 4] * mul, v[h2][8 * q + 5] * mul);
-              a4.w = E::pack(v[h2][8 * q + 6] * mul, v[h2][8 * q + 7] * mul);
-              *reinterpret_cast<uint4*>(drow + 32 * h2 + 8 * q) = a4;
+            for (int q = 0; q < 2; ++q) {  // 16 columns = one 32-byte sector per store
+              uint32_t w8[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) w8[e] = E::pack(v[h2][16 * q + 2 * e] * mul, v[h2][16 * q + 2 * e + 1] * mul);
+              st_global_8w(drow + 32 * h2 + 16 * q, w8, p.dkv_v8);
             }
         }
       }
-      // fold-in: d{K,V}[kj] += sum_g gsc_g * dG_{k,v}[g], summed in fp32 onto the stored value
-      if (ng > 0) {
-#pragma unroll 1
+      // fold-in: d{K,V}[kj] += sum_g gsc_g * dG_{k,v}[g], summed in fp32 onto
+      // the stored value.  The few rows that have global rows (about one per
+      // 128-key tile) are done by the whole warp, one row at a time, lane l
+      // covering D / 32 consecutive columns, so each row costs one round trip
+      // to memory instead of D / 8 dependent ones.  __syncwarp orders the
+      // owner's stores before the other lanes' reads.
+      unsigned fm = __ballot_sync(0xffffffffu, ng > 0);
+      if (fm) __syncwarp();
+      while (fm) {
+        const int src = __ffs(fm) - 1;
+        fm &= fm - 1;
+        constexpr int CPL = D / 32;  // columns per lane: 4 (D = 128) or 2 (D = 64)
+        const int n_s = __shfl_sync(0xffffffffu, ng, src);
+        const int kj_s = __shfl_sync(0xffffffffu, kj, src);
+        int g_s[5];
+        float sc_s[5];
+#pragma unroll
+        for (int gi = 0; gi < 5; ++gi) {
+          g_s[gi] = __shfl_sync(0xffffffffu, gi < ng ? grow[gi] : 0, src);
+          sc_s[gi] = __shfl_sync(0xffffffffu, gi < ng ? gsc[gi] : 0.f, src);
+        }
+        const int c0 = lane * CPL;
+#pragma unroll
         for (int which = 0; which < 2; ++which) {
           const float* dg = which == 0 ? p.dgk : p.dgv;
-          T* drow = which == 0 ? dkrow : dvrow;
-#pragma unroll 1
-          for (int c = 0; c < D; c += 8) {
-            const uint4 cur = *reinterpret_cast<const uint4*>(drow + c);
-            const uint32_t cw[4] = {cur.x, cur.y, cur.z, cur.w};
-            float a[8];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 f = E::unpack(cw[e]);
-              a[2 * e] = f.x;
-              a[2 * e + 1] = f.y;
-            }
-            for (int gi = 0; gi < ng; ++gi) {
-              const float* gr = dg + (gbase + grow[gi]) * D + c;
-              const float4 x0 = *reinterpret_cast<const float4*>(gr);
-              const float4 x1 = *reinterpret_cast<const float4*>(gr + 4);
-              a[0] += gsc[gi] * x0.x; a[1] += gsc[gi] * x0.y; a[2] += gsc[gi] * x0.z; a[3] += gsc[gi] * x0.w;
-              a[4] += gsc[gi] * x1.x; a[5] += gsc[gi] * x1.y; a[6] += gsc[gi] * x1.z; a[7] += gsc[gi] * x1.w;
-            }
-            *reinterpret_cast<uint4*>(drow + c) =
-                make_uint4(E::pack(a[0], a[1]), E::pack(a[2], a[3]), E::pack(a[4], a[5]), E::pack(a[6], a[7]));
+          T* drow = which == 0 ? reinterpret_cast<T*>(p.dk) + tl.b * p.dk_sb + tl.hk * p.dk_sh +
+                                     static_cast<int64_t>(kj_s) * p.dk_ss
+                               : reinterpret_cast<T*>(p.dv) + tl.b * p.dv_sb + tl.hk * p.dv_sh +
+                                     static_cast<int64_t>(kj_s) * p.dv_ss;
+          float a[CPL];
+          if constexpr (CPL == 4) {
+            const uint2 cur = *reinterpret_cast<const uint2*>(drow + c0);
+            const float2 f0 = E::unpack(cur.x), f1 = E::unpack(cur.y);
+            a[0] = f0.x; a[1] = f0.y; a[2] = f1.x; a[3] = f1.y;
+          } else {
+            const float2 f0 = E::unpack(*reinterpret_cast<const uint32_t*>(drow + c0));
+            a[0] = f0.x; a[1] = f0.y;
           }
+#pragma unroll
+          for (int gi = 0; gi < 5; ++gi)
+            if (gi < n_s) {
+              const float* gr = dg + (gbase + g_s[gi]) * D + c0;
+              if constexpr (CPL == 4) {
+                const float4 x = *reinterpret_cast<const float4*>(gr);
+                a[0] += sc_s[gi] * x.x; a[1] += sc_s[gi] * x.y; a[2] += sc_s[gi] * x.z; a[3] += sc_s[gi] * x.w;
+              } else {
+                const float2 x = *reinterpret_cast<const float2*>(gr);
+                a[0] += sc_s[gi] * x.x; a[1] += sc_s[gi] * x.y;
+              }
+            }
+          if constexpr (CPL == 4)
+            *reinterpret_cast<uint2*>(drow + c0) = make_uint2(E::pack(a[0], a[1]), E::pack(a[2], a[3]));
+          else
+            *reinterpret_cast<uint32_t*>(drow + c0) = E::pack(a[0], a[1]);
         }
       }
       PROF_ADD(17, tb);

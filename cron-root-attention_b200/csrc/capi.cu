@@ -66,6 +66,17 @@ int bind_context() {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// True when every row of a 16-bit [dim0, dim1, rows, D] tensor starts on a
+// 32-byte boundary (base and the strides of every dimension longer than 1),
+// so kernels may write its rows with 32-byte stores.
+int rows_aligned32(const void* p, const int64_t* st, int dim0, int dim1, int64_t rows) {
+  if (reinterpret_cast<uintptr_t>(p) & 31) return 0;
+  const int64_t ext[3] = {dim0, dim1, rows};
+  for (int i = 0; i < 3; ++i)
+    if (ext[i] > 1 && (st[i] * 2) % 32 != 0) return 0;
+  return 1;
+}
+
 // Checks one [dim0, dim1, rows, D] tensor description.
 int check_tensor(const char* name, const void* p, const int64_t* st, int dim0, int dim1) {
   if (!p || !st) return fail(CRA_ERR_INVALID_ARGUMENT, "%s: null pointer or strides", name);
@@ -266,6 +277,7 @@ int cra_fwd(const void* q, const void* k, const void* v, const void* g_k, const 
   p.out_sb = o_strides[0];
   p.out_sh = o_strides[1];
   p.out_ss = o_strides[2];
+  p.out_v8 = rows_aligned32(o, o_strides, batch, heads, seq_len);
   p.lse = lse;
   p.delta = nullptr;
   p.B = batch;
@@ -357,6 +369,7 @@ int bwd_impl(const void* q, const void* k, const void* v, const void* o, const v
   qp.out_sb = dq_strides[0];
   qp.out_sh = dq_strides[1];
   qp.out_ss = dq_strides[2];
+  qp.out_v8 = rows_aligned32(dq, dq_strides, batch, heads, seq_len);
   qp.lse = lse2;
   qp.delta = delta;
   qp.B = batch;
@@ -389,6 +402,8 @@ int bwd_impl(const void* q, const void* k, const void* v, const void* o, const v
     kp.dv_sb = dv_strides[0];
     kp.dv_sh = dv_strides[1];
     kp.dv_ss = dv_strides[2];
+    kp.dkv_v8 = rows_aligned32(dk, dk_strides, batch, kv_heads, seq_len) &&
+                rows_aligned32(dv, dv_strides, batch, kv_heads, seq_len);
     kp.dgk = reinterpret_cast<float*>(ws + lay.off_dgk);
     kp.dgv = reinterpret_cast<float*>(ws + lay.off_dgv);
     kp.gsrc = g_src;
@@ -555,6 +570,7 @@ int cra_fwd_shard(const void* q, const void* k, const void* v, const void* g_k, 
   p.out_sb = o_strides[0];
   p.out_sh = o_strides[1];
   p.out_ss = o_strides[2];
+  p.out_v8 = rows_aligned32(o, o_strides, batch, heads, q_len);
   p.lse = lse;
   p.B = batch;
   p.H = heads;

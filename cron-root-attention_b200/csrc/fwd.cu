@@ -367,13 +367,11 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
         tmem_ld_wait();
         if (row_ok) {
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            uint4 pk;
-            pk.x = E::pack(o[8 * u + 0] * inv, o[8 * u + 1] * inv);
-            pk.y = E::pack(o[8 * u + 2] * inv, o[8 * u + 3] * inv);
-            pk.z = E::pack(o[8 * u + 4] * inv, o[8 * u + 5] * inv);
-            pk.w = E::pack(o[8 * u + 6] * inv, o[8 * u + 7] * inv);
-            *reinterpret_cast<uint4*>(orow + 32 * c + 8 * u) = pk;
+          for (int u = 0; u < 2; ++u) {  // 16 columns = one 32-byte sector per store
+            uint32_t w8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) w8[e] = E::pack(o[16 * u + 2 * e] * inv, o[16 * u + 2 * e + 1] * inv);
+            st_global_8w(orow + 32 * c + 16 * u, w8, p.out_v8);
           }
         }
       }

@@ -17,6 +17,7 @@ struct alignas(64) QueryPassParams {
   CUtensorMap tm_do;  // [B, H,   S,  D]   (backward only)
   void* out;          // forward: O;  backward: dQ  (element strides below)
   int64_t out_sb, out_sh, out_ss;
+  int out_v8;         // every output row starts on a 32-byte boundary: 32-byte stores allowed
   float* lse;         // [B, H, S] fp32, natural log (written by fwd, read by bwd)
   const float* delta; // [B, H, S] fp32, rowsum(O * dO) (backward only)
   int B, H, kv_groups, S, W, R, NG, n_qtiles;
@@ -42,6 +43,7 @@ struct alignas(64) KeyPassParams {
   // gradients to fold in (fp32 [B,Hkv,NG,D]) and the relay sources.
   void* dk; void* dv;
   int64_t dk_sb, dk_sh, dk_ss, dv_sb, dv_sh, dv_ss;
+  int dkv_v8;         // every dK / dV row starts on a 32-byte boundary: 32-byte stores allowed
   const float* dgk; const float* dgv;
   const int32_t* gsrc;     // [B, Hkv, NB, TOP_K]
   const float* relay_scale;// [Hkv] relay_log_scale (alpha) per kv head, or null

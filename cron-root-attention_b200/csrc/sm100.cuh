@@ -88,11 +88,17 @@ struct Abort {
 
 // Bounded wait on phase `parity` of barrier `bar`.  Returns false if the CTA
 // is aborting (this wait timed out, or another one did).
+// try_waits between two reads of the clock and of the abort flag
+#ifndef CRA_WAIT_POLLS
+#define CRA_WAIT_POLLS 16
+#endif
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const Abort& ab) {
   if (mbar_try(bar, parity)) return true;
   uint64_t t0 = globaltimer();
   while (true) {
-    if (mbar_try(bar, parity)) return true;
+#pragma unroll 1
+    for (int i = 0; i < CRA_WAIT_POLLS; ++i)
+      if (mbar_try(bar, parity)) return true;
     if (*ab.flag) return false;
     if (globaltimer() - t0 > CRA_WAIT_LIMIT_NS) {
       *ab.flag = 1;
@@ -257,11 +263,56 @@ __device__ __forceinline__ void fadd2(float& a0, float& a1, float b0, float b1) 
       : "f"(b0), "f"(b1));
 }
 
+// Two-lane vector forms on float2 (one f32x2 instruction each).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {  // a * b + c
+  float2 d;
+  asm("{\n\t.reg .b64 x, y, z;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\tmov.b64 z, {%6, %7};\n\t"
+      "fma.rn.f32x2 x, x, y, z;\n\tmov.b64 {%0, %1}, x;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 x, y;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
+      "add.rn.f32x2 x, x, y;\n\tmov.b64 {%0, %1}, x;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 x, y;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
+      "mul.rn.f32x2 x, x, y;\n\tmov.b64 {%0, %1}, x;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
 // Hardware base-2 exponential (MUFU.EX2), flush-to-zero.  ex2(-inf) = +0.
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 32-byte global store (one full sector per thread); 32-byte aligned address.
+__device__ __forceinline__ void st_global_v8(void* p, const uint32_t (&w)[8]) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(w[0]), "r"(w[1]), "r"(w[2]),
+               "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
+}
+
+// Stores 8 words at p: one 32-byte store when v8 (p 32-byte aligned), else
+// two 16-byte stores (p 16-byte aligned).
+__device__ __forceinline__ void st_global_8w(void* p, const uint32_t (&w)[8], bool v8) {
+  if (v8) {
+    st_global_v8(p, w);
+  } else {
+    uint4* q = reinterpret_cast<uint4*>(p);
+    q[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    q[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
 }
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {

@@ -235,3 +235,36 @@ def test_varlen_equal_lengths_batched_matches_per_document(cuda_device):
         assert torch.equal(qs.grad, qd.grad[:, :, s0:s1])
         assert torch.equal(ks.grad, kd.grad[:, :, s0:s1])
         assert torch.equal(vs.grad, vd.grad[:, :, s0:s1])
+
+
+def test_output_rows_only_16_byte_aligned(cuda_device):
+    """Output rows 16- but not 32-byte aligned (row stride 136 elements): the
+    kernels fall back from 32-byte to 16-byte stores; the result equals the
+    one written into a contiguous output, bit for bit."""
+    from cron_root_attention import _lib
+    L = _lib.lib()
+    dev = cuda_device
+    B, H, S, D = 1, 2, 2600, 128
+    q, k, v = (t.to(dev) for t in inputs(B, H, H, S, D, torch.bfloat16, 38))
+    W = L.cra_window(S)
+    NB = (S + W - 1) // W
+    NG = L.cra_global_rows(S, 1, 2)
+    gk = torch.empty(B, H, NG, D, device=dev, dtype=torch.bfloat16)
+    gv = torch.empty_like(gk)
+    gsrc = torch.empty(B, H, NB, 2, device=dev, dtype=torch.int32)
+    st = _lib.strides3
+    s = torch.cuda.current_stream(dev).cuda_stream
+    _lib.check(L.cra_relay_build(k.data_ptr(), v.data_ptr(), st(k), st(v), B, H, S, D, 1, 1, 2, None,
+                                 gk.data_ptr(), gv.data_ptr(), gsrc.data_ptr(), s), "relay")
+    outs = []
+    for wide in (D, 136):
+        buf = torch.zeros(B, H, S, wide, device=dev, dtype=torch.bfloat16)
+        o = buf[..., :D]
+        lse = torch.empty(B, H, S, device=dev, dtype=torch.float32)
+        _lib.check(L.cra_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), gk.data_ptr(), gv.data_ptr(), st(q), st(k),
+                             st(v), B, H, H, S, D, 1, 1, 2, ctypes.c_float(D ** -0.5), o.data_ptr(), st(o),
+                             lse.data_ptr(), None, s), "fwd")
+        outs.append((buf, o.clone()))
+    torch.cuda.synchronize(dev)
+    assert torch.equal(outs[0][1], outs[1][1])
+    assert torch.count_nonzero(outs[1][0][..., D:]) == 0  # nothing written past the row
