@@ -224,10 +224,11 @@ TRAFFIC_H8 = {
     "reduce_kernel": None,
     "keylocal_kernel": None,
     "dq_kernel": None,
+    "dq_convert_kernel": None,
 }
 
 
-def kernel_work(name: str, W: int, NG: int):
+def kernel_work(name: str, W: int, NG: int, fused: bool = False):
     """(bound, algorithmic work per launch, unit) of each kernel at B x H x S x D.
     Attention kernels: the useful (unmasked) MMA FLOPs they perform -- 2 D per
     visible pair per GEMM; forward 2 GEMMs, dQ pass 3 (S, dP, dQ), key passes
@@ -244,15 +245,20 @@ def kernel_work(name: str, W: int, NG: int):
         return "tensor", 4.0 * D * pairs_per_head() * bh, "TFLOP/s"
     if name == "dq_kernel":
         return "tensor", 6.0 * D * pairs_per_head() * bh, "TFLOP/s"
+    # key passes: 4 GEMMs (S, dP, dV, dK); cra_bwd_fused adds dQ there (5)
+    gemms = 5 if (fused and D == 128) else 4
     if name == "keyglobal_kernel":
-        return "tensor", 8.0 * D * glob * bh, "TFLOP/s"
+        return "tensor", 2.0 * gemms * D * glob * bh, "TFLOP/s"
     if name == "keylocal_kernel":
-        return "tensor", 8.0 * D * local * bh, "TFLOP/s"
+        return "tensor", 2.0 * gemms * D * local * bh, "TFLOP/s"
+    if name == "dq_convert_kernel":  # fp32 accumulator read, dQ written
+        return "hbm", (4 + eb) * S * D * bh, "GB/s"
     if name == "relay_build_kernel":  # K read once + chosen K / V rows read and written as G
         return "hbm", (S * D * eb + 4 * NG * D * eb) * bh, "GB/s"
     if name == "delta_kernel":  # O, dO read; lse read; lse2, delta written (fp32, padded)
         spad = math.ceil(S / 128) * 128
-        return "hbm", (2 * S * D * eb + 4 * S + 8 * spad) * bh, "GB/s"
+        zero = 4 * spad * D if (fused and D == 128) else 0  # fused: the dQ accumulator is zeroed
+        return "hbm", (2 * S * D * eb + 4 * S + 8 * spad + zero) * bh, "GB/s"
     if name == "reduce_kernel":  # n_split partials of dG_k, dG_v read, dG written (fp32)
         return "hbm", None, "GB/s"
     return "other", None, None
@@ -359,14 +365,31 @@ def run_ours(args, rank, world, local_rank):
             q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(), lse.data_ptr(), gk.data_ptr(),
             gv.data_ptr(), gsrc.data_ptr(), st(q), st(k), st(v), st(o), st(do), B, H, H, S, D, 1, 1, 2,
             ctypes.c_float(D ** -0.5), None, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), st(dq), st(dk), st(dv),
-            None, ws.data_ptr(), ws_bytes, err, sp, ms_arr, names, nmax, ctypes.byref(nk)), "cra_bwd_kernel_times")
+            None, ws.data_ptr(), ws_bytes, err, sp, ms_arr, names, nmax, ctypes.byref(nk), 0), "cra_bwd_kernel_times")
         if it >= 3:
             for i in range(nk.value):
                 samples.setdefault(names[i].decode(), []).append(ms_arr[i])
     for name, xs in samples.items():
         kern_ms[name] = max_over_ranks(statistics.median(xs))
     n_bwd_kernels = nk.value
+    # the alternative backward (cra_bwd_fused: dQ inside the key passes by
+    # fp32 atomic adds, no dQ pass), timed the same way for comparison
+    fws_bytes = L.cra_bwd_fused_workspace_bytes(B, H, H, S, D, 1, 2)
+    del ws
+    ws = torch.empty(fws_bytes, device=dev, dtype=torch.uint8)
+    fsamples = {}
+    for it in range(3 + args.steps):
+        _lib.check(L.cra_bwd_kernel_times(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(), lse.data_ptr(), gk.data_ptr(),
+            gv.data_ptr(), gsrc.data_ptr(), st(q), st(k), st(v), st(o), st(do), B, H, H, S, D, 1, 1, 2,
+            ctypes.c_float(D ** -0.5), None, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), st(dq), st(dk), st(dv),
+            None, ws.data_ptr(), fws_bytes, err, sp, ms_arr, names, nmax, ctypes.byref(nk), 1), "fused kernel times")
+        if it >= 3:
+            for i in range(nk.value):
+                fsamples.setdefault(names[i].decode(), []).append(ms_arr[i])
+    fused_ms = {n: max_over_ranks(statistics.median(xs)) for n, xs in fsamples.items()}
     del ws, dq, dk, dv
+    bwd_ms = sum(v for n, v in kern_ms.items() if n not in ("fwd_kernel", "relay_build_kernel"))
 
     # --- end to end through the public API with host buffers: every step copies
     # q, k, v, dO from pinned memory to the device, runs fwd + bwd, and copies
@@ -470,6 +493,11 @@ def run_ours(args, rank, world, local_rank):
                    "flops_per_step": f"fwd {f_fwd / 1e9:.3f} GFLOP + bwd {f_bwd / 1e9:.3f} GFLOP per GPU"},
         "roofline": roofline,
         "kernels": kernels,
+        "bwd_alternatives": {
+            "three_pass": {"entry": "cra_bwd (used by the API)", "kernels_ms": bwd_ms,
+                           "dq": "separate dQ pass, fixed summation order"},
+            "fused": {"entry": "cra_bwd_fused", "kernels_ms": sum(fused_ms.values()), "per_kernel_ms": fused_ms,
+                      "dq": "added by the key passes with fp32 atomics (order varies between calls)"}},
         "e2e": {"value": world * (f_fwd + f_bwd) / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
                 "ms_per_step": ms_e2e, "h2d_bytes_per_step": 4 * nbytes, "d2h_bytes_per_step": 3 * nbytes,
                 "steps": n_e2e, "copies": "pipelined across steps on separate H2D / D2H streams",

@@ -37,15 +37,20 @@ _SIGNATURES = {
     "cra_relay_build_shard": (_i, [_vp, _vp, _i64p, _i64p, _i, _i, ctypes.c_int64, ctypes.c_int64, _i, _i, _i, _i, _i,
                                    _vp, _vp, _vp, _vp, _vp]),
     "cra_fwd_shard": (_i, [_vp, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _i, _i, _i, ctypes.c_int64, ctypes.c_int64,
-                           _i, ctypes.c_int64, _i, _i, _i, _i, _i, _f, _vp, _i64p, _vp, _vp, _vp]),
+                           _i, ctypes.c_int64, _i, _vp, _vp, _i64p, _i64p, ctypes.c_int64, _i,
+                           _i, _i, _i, _i, _f, _vp, _i64p, _vp, _vp, _vp]),
     "cra_bwd_workspace_bytes": (ctypes.c_size_t, [_i, _i, _i, _i, _i, _i, _i]),
+    "cra_bwd_fused_workspace_bytes": (ctypes.c_size_t, [_i, _i, _i, _i, _i, _i, _i]),
     "cra_bwd": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _i64p, _i64p,
                      _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _vp, _vp,
                      ctypes.c_size_t, _vp, _vp]),
     "cra_bwd_kernel_times": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _i64p, _i64p,
                                   _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _vp,
                                   _vp, ctypes.c_size_t, _vp, _vp, ctypes.POINTER(_f),
-                                  ctypes.POINTER(ctypes.c_char_p), _i, ctypes.POINTER(_i)]),
+                                  ctypes.POINTER(ctypes.c_char_p), _i, ctypes.POINTER(_i), _i]),
+    "cra_bwd_fused": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _i64p, _i64p,
+                                   _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p,
+                                   _vp, _vp, ctypes.c_size_t, _vp, _vp]),
     "cra_bwd_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _i64p, _i64p,
                              _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _vp,
                              _vp, _vp]),

@@ -13,7 +13,8 @@ Two ways to spread the work, matching how the attention decomposes:
       WHOLE sequence.
   Each rank builds the global rows of its own blocks, then one all-gather
   (NCCL over NVLink on GPUs) assembles the full list in every rank's memory;
-  the halo rows travel in a second small all-gather.  Everything lands in
+  the halo rows go point to point to the next rank only, which reads them
+  (with its own first rows) from a small edge copy.  Everything lands in
   local HBM before the forward kernel reads it.
 
 Reference: the reference package is single-GPU (no collectives); the
@@ -126,7 +127,10 @@ class LibcraShardOps:
                                                _stream_ptr(k.device)), "cra_relay_build_shard")
         return gk, gv
 
-    def forward_shard(self, q, k, v, gk, gv, seq_len, q_begin, kv_begin, use_relay, top_k):
+    def forward_shard(self, q, k, v, gk, gv, seq_len, q_begin, kv_begin, use_relay, top_k, edge=None):
+        """Forward of one shard.  ``edge`` = (k_edge, v_edge, edge_begin): a
+        small copy of the halo rows and the shard's first rows; then k / v
+        are the shard's own rows (kv_begin = q_begin)."""
         from . import _lib
         from .core import _dtype_code, _err_word, _stream_ptr
         L = _lib.lib()
@@ -135,12 +139,17 @@ class LibcraShardOps:
         o = torch.empty_like(q)
         lse = torch.empty(B, H, q_len, device=q.device, dtype=torch.float32)
         st = _lib.strides3
+        if edge is not None:
+            ke, ve, e0 = edge
+            eargs = (ke.data_ptr(), ve.data_ptr(), st(ke), st(ve), e0, ke.shape[2])
+        else:
+            eargs = (None, None, None, None, 0, 0)
         with torch.cuda.device(q.device):
             _lib.check(L.cra_fwd_shard(q.data_ptr(), k.data_ptr(), v.data_ptr(), gk.data_ptr(), gv.data_ptr(),
-                                       st(q), st(k), st(v), B, H, Hkv, seq_len, q_begin, q_len, kv_begin, kv_len, D,
-                                       _dtype_code(q.dtype), int(use_relay), top_k, ctypes.c_float(D ** -0.5),
-                                       o.data_ptr(), st(o), lse.data_ptr(), _err_word(q.device).data_ptr(),
-                                       _stream_ptr(q.device)), "cra_fwd_shard")
+                                       st(q), st(k), st(v), B, H, Hkv, seq_len, q_begin, q_len, kv_begin, kv_len,
+                                       *eargs, D, _dtype_code(q.dtype), int(use_relay), top_k,
+                                       ctypes.c_float(D ** -0.5), o.data_ptr(), st(o), lse.data_ptr(),
+                                       _err_word(q.device).data_ptr(), _stream_ptr(q.device)), "cra_fwd_shard")
         return o
 
 
@@ -169,8 +178,8 @@ def seq_parallel_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, seq_
 
     q, k, v: this rank's rows, [B, H, end - begin, D] with (begin, end) =
     seq_shard(seq_len, world, rank).  Returns this rank's output rows.
-    Collectives: two all-gathers (global rows, then the halo rows); no
-    data-dependent host synchronisation.  Without an initialized process
+    Collectives: one all-gather (global rows) and one neighbour send/recv
+    (halo rows); no data-dependent host synchronisation.  Without an initialized process
     group (and no ``group`` given) it runs as a single rank.
     """
     if group is None and not (dist.is_available() and dist.is_initialized()):
@@ -190,27 +199,36 @@ def seq_parallel_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, seq_
     rows = [((e - b + W - 1) // W) * R for b, e in (seq_shard(seq_len, world, r, relay_top_k) for r in range(world))]
     gk = _all_gather_padded(gk, 2, rows, group)
     gv = _all_gather_padded(gv, 2, rows, group)
-    # 2) halo: the last W - 1 K/V rows of the previous rank
+    # 2) halo: the last W - 1 K/V rows of the previous rank, sent to the next
+    # rank only (point to point); the receiver builds a small edge copy --
+    # halo rows followed by its own first W + 256 rows -- which the query
+    # tiles whose window reaches into the halo read, so the shard's own K / V
+    # are used in place (no copy of the whole shard)
     halo = W - 1
-    tail_k = k[:, :, max(0, k.shape[2] - halo):]
-    tail_v = v[:, :, max(0, v.shape[2] - halo):]
-    sizes = [min(halo, e - b) for b, e in (seq_shard(seq_len, world, r, relay_top_k) for r in range(world))]
-    hk = _all_gather_padded(tail_k, 2, sizes, group)
-    hv = _all_gather_padded(tail_v, 2, sizes, group)
-    if rank > 0:
-        off = sum(sizes[:rank - 1])
-        n = sizes[rank - 1]
-        # halo rows in front of this rank's rows: one allocation and two plain
-        # copies each (a concatenation along the sequence dimension of
-        # GB-sized tensors ran far below HBM bandwidth)
-        kk = k.new_empty(k.shape[0], k.shape[1], n + k.shape[2], k.shape[3])
-        vv = v.new_empty(v.shape[0], v.shape[1], n + v.shape[2], v.shape[3])
-        kk[:, :, :n].copy_(hk.narrow(2, off, n))
-        kk[:, :, n:].copy_(k)
-        vv[:, :, :n].copy_(hv.narrow(2, off, n))
-        vv[:, :, n:].copy_(v)
-        kv_begin = begin - n
-    else:
-        kk, vv, kv_begin = k.contiguous(), v.contiguous(), 0
-    return ops.forward_shard(q.contiguous(), kk, vv, gk.contiguous(), gv.contiguous(), seq_len, begin, kv_begin,
+    n_in = min(halo, begin) if rank > 0 else 0
+    if world > 1:
+        ops_p2p = []
+        tail = None
+        if rank + 1 < world:
+            tail = torch.cat([k[:, :, max(0, k.shape[2] - halo):], v[:, :, max(0, v.shape[2] - halo):]], dim=1)
+            ops_p2p.append(dist.P2POp(dist.isend, tail.contiguous(), (rank + 1) if group is None
+                                      else dist.get_global_rank(group, rank + 1), group))
+        recv = None
+        if rank > 0:
+            prev_b, prev_e = seq_shard(seq_len, world, rank - 1, relay_top_k)
+            n_in = min(halo, prev_e - prev_b)
+            recv = k.new_empty(k.shape[0], 2 * k.shape[1], n_in, k.shape[3])
+            ops_p2p.append(dist.P2POp(dist.irecv, recv, (rank - 1) if group is None
+                                      else dist.get_global_rank(group, rank - 1), group))
+        for req in dist.batch_isend_irecv(ops_p2p):
+            req.wait()
+    qc, kc, vc = q.contiguous(), k.contiguous(), v.contiguous()
+    if rank > 0 and n_in > 0:
+        Hkv = k.shape[1]
+        X = min(W + 256, k.shape[2])
+        ke = torch.cat([recv[:, :Hkv], k[:, :, :X]], dim=2).contiguous()
+        ve = torch.cat([recv[:, Hkv:], v[:, :, :X]], dim=2).contiguous()
+        return ops.forward_shard(qc, kc, vc, gk.contiguous(), gv.contiguous(), seq_len, begin, begin, use_relay,
+                                 relay_top_k, edge=(ke, ve, begin - n_in))
+    return ops.forward_shard(qc, kc, vc, gk.contiguous(), gv.contiguous(), seq_len, begin, 0 if rank == 0 else begin,
                              use_relay, relay_top_k)

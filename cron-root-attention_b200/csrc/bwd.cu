@@ -8,7 +8,8 @@
 //   relay-row gradients land on their source tokens (core.py:2811-2815).
 //
 // Kernels, in launch order:
-//   delta_kernel     Di and lse*log2(e), padded to whole 128-query tiles.
+//   delta_kernel     -Di and -lse*log2(e), padded to whole 128-query tiles;
+//                    fused: also zeroes the fp32 dQ accumulator.
 //   keyglobal_kernel one CTA per (128 global rows, query split): dG_k / dG_v
 //                    over every query that sees the rows; fp32 partials per
 //                    split (no atomics).
@@ -19,9 +20,17 @@
 //                    over the local band, then folds in dG of the tile's
 //                    strided key and of every relay row whose source lies in
 //                    the tile, and stores.
+//   then either (cra_bwd_fused, head_dim 128)
+//   dq_convert_kernel dQ = scale * accumulator, to the output dtype: the two
+//                    key passes have already added dS K of every unit into
+//                    the fp32 accumulator (a fifth GEMM per unit, dQ^T = K^T
+//                    dS^T, read out of TMEM and added with fp32 atomics), so
+//                    the scores are recomputed once instead of twice;
+//   or (cra_bwd, the default: every sum in a fixed order)
 //   dq_kernel        persistent (one CTA per SM) over 128-query tiles: dQ over
 //                    band + global prefix.
-// The result is deterministic: every sum has a fixed order.
+// dK, dV and dG always have a fixed summation order; only the fused dQ does
+// not (fp32 atomic adds).
 //
 // The attention kernels use the warp roles of the forward (fwd.cu): warp 0
 // TMA producer, warp 1 tcgen05 issuer (whole warp, one elected lane) + TMEM
@@ -84,6 +93,57 @@ __device__ __forceinline__ void key_softmax_chunk(const float (&s)[32], const fl
     body(std::true_type{});
 }
 
+// Fused backward: row r (key) of the unit's dS^T, chunk c (queries [32c,
+// 32c+32), 16 packed pairs), into the [128 x 64] 16-bit dS^T buffer in the
+// 128-byte swizzled layout of an MN-major UMMA operand (16-byte piece j of
+// row r at j ^ (r & 7)).
+__device__ __forceinline__ void store_ds_chunk(uint8_t* ds, int r, int c, const uint32_t (&dpk)[16]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int piece = (4 * c + i) ^ (r & 7);
+    *reinterpret_cast<uint4*>(ds + r * 128 + piece * 16) =
+        make_uint4(dpk[4 * i], dpk[4 * i + 1], dpk[4 * i + 2], dpk[4 * i + 3]);
+  }
+}
+
+// Fused backward: dQ^T[d, q] = sum_j K[j, d] dS^T[j, q] for one 64-query
+// unit into TMEM (lanes = the 128 head dims, 64 columns = queries): A = K^T
+// (the key tile in shared memory read MN-major), B = dS^T (MN-major), 8
+// K-steps of 16 keys.  Whole warp, one elected lane.
+template <bool BF16>
+__device__ __forceinline__ void mma_dqt(uint32_t d_tmem, uint32_t k_smem, uint32_t ds_smem) {
+  constexpr uint32_t ID = idesc_f16(BF16, 128, kUnit, true, true);
+  const uint64_t a = sdesc(k_smem, kTile * 128, 1024), b = sdesc(ds_smem, kTile * 128, 1024);
+#pragma unroll
+  for (int kk = 0; kk < kTile / 16; ++kk)
+    mma_ss_w(d_tmem, a + ((kk * 16 * 128) >> 4), b + ((kk * 16 * 128) >> 4), ID, kk > 0 ? 1u : 0u);
+}
+
+// Fused backward: reads dQ^T of a unit out of TMEM (this thread: head dim r,
+// 64 queries), frees the slot, then adds it into the fp32 dQ accumulator
+// rows q0 .. q0 + 63 (one warp instruction covers 32 consecutive dims of a
+// row).  The scale is applied when the accumulator is converted.
+__device__ __forceinline__ bool drain_dqt(uint32_t taddr, uint32_t full_bar, uint32_t parity, uint32_t free_bar,
+                                          float* acc_row0, int D, const Abort& ab) {
+  if (!mbar_wait(full_bar, parity, ab)) return false;
+  tc_fence_after();
+  float a[32], c[32];
+  tmem_ld32(taddr, a);
+  tmem_ld32(taddr + 32, c);
+  tmem_ld_wait();
+  tc_fence_before();
+  mbar_arrive(free_bar);
+#ifdef CRA_PROBE_NORED  // measurement probe: no accumulation (wrong dQ)
+  if (a[0] == 12345.f && c[0] == 54321.f) acc_row0[0] = 1.f;
+#else
+#pragma unroll
+  for (int j = 0; j < 32; ++j) atomicAdd(acc_row0 + static_cast<int64_t>(j) * D, a[j]);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) atomicAdd(acc_row0 + static_cast<int64_t>(j + 32) * D, c[j]);
+#endif
+  return true;
+}
+
 // ===========================================================================
 // delta: ndelta = -rowsum(O * dO);  nlse2 = -lse * log2(e).  Both are stored
 // negated so the softmax passes add them with one packed f32x2 instruction
@@ -94,7 +154,7 @@ __global__ void __launch_bounds__(256) delta_kernel(const void* __restrict__ op,
                                                     int64_t o_sb, int64_t o_sh, int64_t o_ss, int64_t d_sb,
                                                     int64_t d_sh, int64_t d_ss, const float* __restrict__ lse, int H,
                                                     int S, int Spad, float* __restrict__ lse2,
-                                                    float* __restrict__ delta) {
+                                                    float* __restrict__ delta, float* __restrict__ dq_acc) {
   using E = Elt<BF16>;
   using T = typename E::T;
   constexpr int LPR = D / 8, RPW = 32 / LPR;
@@ -119,6 +179,11 @@ __global__ void __launch_bounds__(256) delta_kernel(const void* __restrict__ op,
   }
 #pragma unroll
   for (int off = LPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (dq_acc && row < Spad) {  // fused backward: the dQ accumulator starts at zero
+    float4* z = reinterpret_cast<float4*>(dq_acc + (static_cast<int64_t>(bh) * Spad + row) * D + part * 8);
+    z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+    z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   if (part == 0 && row < Spad) {
     const int64_t i = static_cast<int64_t>(bh) * Spad + row;
     delta[i] = row < S ? -acc : 0.f;
@@ -560,18 +625,22 @@ extern "C" __attribute__((visibility("default"))) int cra_kl_prof(unsigned long 
 // read it were issued; MMAs issued by one warp execute in issue order, so no
 // completion wait is needed (one would drain the tensor pipe every unit).
 // ===========================================================================
-template <int D>
+template <int D, bool FUSED>
 struct KeyCfg {
   static constexpr int TB = kTile * D * 2;         // K or V tile
   static constexpr int UB = kUnit * D * 2;         // Q or dO unit
-  static constexpr int NSQ = (D == 128) ? 4 : 8;   // Q/dO unit stages
+  static constexpr int NSQ = FUSED ? 3 : (D == 128) ? 4 : 8;  // Q/dO unit stages
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + TB;
   static constexpr int OFF_Q = OFF_V + TB;         // stage s: Q at OFF_Q + 2 s UB, dO after it
   static constexpr int OFF_LSE = OFF_Q + NSQ * 2 * UB;  // stage s: lse2[64], delta[64]
-  static constexpr int OFF_BAR = OFF_LSE + NSQ * 2 * kUnit * 4;
+  // fused: dS^T of the units of parity s, [128 keys x 64 queries] 16-bit
+  static constexpr int OFF_DS = (OFF_LSE + NSQ * 2 * kUnit * 4 + 1023) / 1024 * 1024;
+  static constexpr int DSB = kTile * kUnit * 2;
+  static constexpr int OFF_BAR = FUSED ? OFF_DS + 2 * DSB : OFF_LSE + NSQ * 2 * kUnit * 4;
   static constexpr int B_KVFULL = 0, B_QFULL = 1, B_QEMPTY = 1 + NSQ, B_SFULL = 1 + 2 * NSQ, B_PFULL = B_SFULL + 2,
-                       B_DONE = B_PFULL + 2, B_DRAIN = B_DONE + 1, N_BAR = B_DRAIN + 1;
+                       B_DONE = B_PFULL + 2, B_DRAIN = B_DONE + 1, B_DQFULL = B_DRAIN + 1, B_DQFREE = B_DQFULL + 2,
+                       N_BAR = B_DQFREE + 2;
   static constexpr int OFF_MISC = OFF_BAR + N_BAR * 8;
   static constexpr int SMEM = OFF_MISC + 16 + 1024;
   // TMEM: slot s -> S^T at 128 s, dP^T at 128 s + 64 (fp32, 64 columns each);
@@ -582,9 +651,9 @@ struct KeyCfg {
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
-template <int D, bool BF16>
+template <int D, bool BF16, bool FUSED>
 __global__ void __launch_bounds__(320, 1) keyglobal_kernel(const __grid_constant__ KeyPassParams p) {
-  using C = KeyCfg<D>;
+  using C = KeyCfg<D, FUSED>;
   using E = Elt<BF16>;
   using T = typename E::T;
   extern __shared__ uint8_t smem_raw[];
@@ -625,6 +694,10 @@ __global__ void __launch_bounds__(320, 1) keyglobal_kernel(const __grid_constant
       mbar_init(BAR(C::B_PFULL + s), 128);
     }
     mbar_init(BAR(C::B_DONE), 1);
+    for (int q = 0; q < 2; ++q) {
+      mbar_init(BAR(C::B_DQFULL + q), 1);
+      mbar_init(BAR(C::B_DQFREE + q), 128);
+    }
     mbar_init(BAR(C::B_DRAIN), 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -678,6 +751,7 @@ __global__ void __launch_bounds__(320, 1) keyglobal_kernel(const __grid_constant
       constexpr uint32_t ID_G = idesc_f16(BF16, kTile, D, false, true);
       const uint32_t ks = sbase + C::OFF_K, vs = sbase + C::OFF_V;
       bool ok = warp_wait(BAR(C::B_KVFULL), 0, ab);
+      auto issue_dqt = [&](uint32_t d_tmem, uint32_t k_smem, uint32_t ds_smem) { mma_dqt<BF16>(d_tmem, k_smem, ds_smem); };
       auto issue_kv = [&](int i) -> bool {
         const int st = i % C::NSQ, sl = i & 1;
         if (!warp_wait(BAR(C::B_PFULL + sl), (i >> 1) & 1, ab)) return false;
@@ -692,13 +766,19 @@ __global__ void __launch_bounds__(320, 1) keyglobal_kernel(const __grid_constant
                  (i > 0 || kk > 0) ? 1u : 0u);
         }
         mma_commit_w(BAR(C::B_QEMPTY + st));
+        if constexpr (FUSED) {  // dQ^T of the unit into its (read) score slot
+          issue_dqt(tmem + 128 * sl, ks, sbase + C::OFF_DS + sl * C::DSB);
+          mma_commit_w(BAR(C::B_DQFULL + sl));
+        }
         return true;
       };
       for (int u = 0; ok && u < nU; ++u) {
         const int st = u % C::NSQ, sl = u & 1;
         // slot sl was last read by the dV / dK products of unit u - 2, issued
-        // before this S^T / dP^T (in-order execution)
-        if (!warp_wait(BAR(C::B_QFULL + st), (u / C::NSQ) & 1, ab)) {
+        // before this S^T / dP^T (in-order execution); fused, it then held
+        // dQ^T of unit u - 2 until the softmax warps read it out
+        if (!warp_wait(BAR(C::B_QFULL + st), (u / C::NSQ) & 1, ab) ||
+            (FUSED && u >= 2 && !warp_wait(BAR(C::B_DQFREE + sl), ((u >> 1) - 1) & 1, ab))) {
           ok = false;
           break;
         }
@@ -765,10 +845,19 @@ __global__ void __launch_bounds__(320, 1) keyglobal_kernel(const __grid_constant
         // S^T / dP^T, already consumed (columns [0, 32c+32) have been read)
         tmem_st16(scol + 16 * c, ppk);
         tmem_st16(scol + 64 + 16 * c, dpk);
+        if constexpr (FUSED) store_ds_chunk(smem + C::OFF_DS + w * C::DSB, r, c, dpk);
       }
       tmem_st_wait();
+      if constexpr (FUSED) fence_proxy_async();  // dS^T stores -> the dQ^T MMA
       tc_fence_before();
       mbar_arrive(BAR(C::B_PFULL + w));
+      if constexpr (FUSED) {
+        float* acc = p.dq_acc + ((static_cast<int64_t>(b) * p.H + h) * Spad + q0) * D + r;
+        if (!drain_dqt(scol, BAR(C::B_DQFULL + w), (u >> 1) & 1, BAR(C::B_DQFREE + w), acc, D, ab)) {
+          ok = false;
+          break;
+        }
+      }
     }
     // ------------------------------------------------------------ epilogue
     // warpgroup 0 writes dG_k partials, warpgroup 1 dG_v partials
@@ -820,18 +909,20 @@ __global__ void __launch_bounds__(320, 1) keyglobal_kernel(const __grid_constant
 //     waits for it (ACCFREE).
 // Warps: 0 producer, 1 MMA issuer, 2-5 / 6-9 softmax, 10-13 epilogue.
 // ===========================================================================
-template <int D>
+template <int D, bool FUSED>
 struct KeyLocalCfg {
   static constexpr int TB = kTile * D * 2;         // K or V tile
   static constexpr int UB = kUnit * D * 2;         // Q or dO unit
-  static constexpr int NSQ = (D == 128) ? 3 : 8;   // Q/dO unit stages
+  static constexpr int NSQ = FUSED ? 2 : (D == 128) ? 3 : 8;  // Q/dO unit stages
   static constexpr int OFF_KV = 0;                 // buffer b: K at 2 b TB, V at (2 b + 1) TB
   static constexpr int OFF_Q = 4 * TB;             // stage s: Q at OFF_Q + 2 s UB, dO after it
   static constexpr int OFF_LSE = OFF_Q + NSQ * 2 * UB;  // stage s: lse2[64], delta[64]
-  static constexpr int OFF_BAR = OFF_LSE + NSQ * 2 * kUnit * 4;
+  static constexpr int OFF_DS = (OFF_LSE + NSQ * 2 * kUnit * 4 + 1023) / 1024 * 1024;  // fused: dS^T, 2 buffers
+  static constexpr int DSB = kTile * kUnit * 2;
+  static constexpr int OFF_BAR = FUSED ? OFF_DS + 2 * DSB : OFF_LSE + NSQ * 2 * kUnit * 4;
   static constexpr int B_KVFULL = 0, B_KVEMPTY = 2, B_QFULL = 4, B_QEMPTY = 4 + NSQ, B_SFULL = 4 + 2 * NSQ,
                        B_PFULL = B_SFULL + 2, B_ACCFULL = B_PFULL + 2, B_ACCFREE = B_ACCFULL + 1,
-                       B_DRAIN = B_ACCFREE + 1, N_BAR = B_DRAIN + 1;
+                       B_DRAIN = B_ACCFREE + 1, B_DQFULL = B_DRAIN + 1, B_DQFREE = B_DQFULL + 2, N_BAR = B_DQFREE + 2;
   static constexpr int OFF_MISC = OFF_BAR + N_BAR * 8;
   static constexpr int SMEM = OFF_MISC + 16 + 1024;
   static constexpr int COL_DV = 256, COL_DK = 256 + D;  // slots at 0 and 128 as in KeyCfg
@@ -863,9 +954,9 @@ struct KeyLocalTile {
 #define PROF_ARR g_kl_prof
 #endif
 
-template <int D, bool BF16>
+template <int D, bool BF16, bool FUSED>
 __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant__ KeyPassParams p) {
-  using C = KeyLocalCfg<D>;
+  using C = KeyLocalCfg<D, FUSED>;
   using E = Elt<BF16>;
   using T = typename E::T;
   extern __shared__ uint8_t smem_raw[];
@@ -897,6 +988,10 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
     }
     mbar_init(BAR(C::B_ACCFULL), 1);
     mbar_init(BAR(C::B_ACCFREE), 128);
+    for (int q = 0; q < 2; ++q) {
+      mbar_init(BAR(C::B_DQFULL + q), 1);
+      mbar_init(BAR(C::B_DQFREE + q), 128);
+    }
     mbar_init(BAR(C::B_DRAIN), 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -976,6 +1071,11 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
       }
       mma_commit_w(BAR(C::B_QEMPTY + st));
       if (last) mma_commit_w(BAR(C::B_ACCFULL));
+      if constexpr (FUSED) {  // dQ^T of the unit into its (read) score slot; reads the tile's K
+        mma_dqt<BF16>(tmem + 128 * sl, sbase + C::OFF_KV + 2 * (iti & 1) * C::TB, sbase + C::OFF_DS + sl * C::DSB);
+        mma_commit_w(BAR(C::B_DQFULL + sl));
+        if (last) mma_commit_w(BAR(C::B_KVEMPTY + (iti & 1)));  // K / V of the tile: last reader issued
+      }
       return true;
     };
     PROF_T(tstart);
@@ -995,6 +1095,7 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
         // before this S^T / dP^T (in-order execution)
         PROF_T(tq);
         if (!warp_wait(BAR(C::B_QFULL + st), (u / C::NSQ) & 1, ab)) { ok = false; break; }
+        if (FUSED && u >= 2 && !warp_wait(BAR(C::B_DQFREE + sl), ((u >> 1) - 1) & 1, ab)) { ok = false; break; }
         PROF_ADD(7, tq);
         tc_fence_after();
         const uint32_t qa = sbase + C::OFF_Q + st * 2 * C::UB;
@@ -1007,7 +1108,7 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
           mma_ss_w(tmem + 128 * sl + 64, vd + ko, dd + qo, ID_S, kk > 0 ? 1u : 0u);
         }
         mma_commit_w(BAR(C::B_SFULL + sl));
-        if (ul == tl.nU - 1) mma_commit_w(BAR(C::B_KVEMPTY + kb));  // K / V of this tile: last reader issued
+        if (!FUSED && ul == tl.nU - 1) mma_commit_w(BAR(C::B_KVEMPTY + kb));  // K / V of this tile: last reader issued
         if (u > 0 && !issue_kv(u - 1, pit, pfirst, pit != i)) { ok = false; break; }
         pit = i;
         pfirst = ul == 0;
@@ -1070,10 +1171,19 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
           // S^T / dP^T, already consumed (columns [0, 32c+32) have been read)
           tmem_st16(scol + 16 * c, ppk);
           tmem_st16(scol + 64 + 16 * c, dpk);
+          if constexpr (FUSED) store_ds_chunk(smem + C::OFF_DS + w * C::DSB, r, c, dpk);
         }
         tmem_st_wait();
+        if constexpr (FUSED) fence_proxy_async();  // dS^T stores -> the dQ^T MMA
         tc_fence_before();
         mbar_arrive(BAR(C::B_PFULL + w));
+        if constexpr (FUSED) {
+          float* acc = p.dq_acc + ((static_cast<int64_t>(tl.b) * p.H + h) * Spad + q0) * D + r;
+          if (!drain_dqt(scol, BAR(C::B_DQFULL + w), (uu >> 1) & 1, BAR(C::B_DQFREE + w), acc, D, ab)) {
+            ok = false;
+            break;
+          }
+        }
         PROF_ADD(13, tb);
       }
     }
@@ -1287,9 +1397,91 @@ static cudaError_t set_smem(K kern, int bytes) {
   return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
+// Fused backward: dQ = scale * dQ accumulator, rounded to the output dtype.
+// One thread per 8 elements of a row.
+template <int D, bool BF16>
+__global__ void __launch_bounds__(256) dq_convert_kernel(const float* __restrict__ acc, void* __restrict__ dq,
+                                                         int64_t sb, int64_t sh, int64_t ss, int64_t n_rows, int H,
+                                                         int S, int Spad, float scale) {
+  using E = Elt<BF16>;
+  constexpr int PR = D / 8;  // threads per row
+  const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  const int64_t row = i / PR;  // over B * H * S rows
+  if (row >= n_rows) return;
+  const int part = static_cast<int>(i % PR);
+  const int64_t bh = row / S;
+  const int srow = static_cast<int>(row % S);
+  const float4* a = reinterpret_cast<const float4*>(acc + (bh * Spad + srow) * D + part * 8);
+  const float4 x = a[0], y = a[1];
+  const int b = static_cast<int>(bh / H), h = static_cast<int>(bh % H);
+  typename E::T* out = reinterpret_cast<typename E::T*>(dq) + b * sb + h * sh + static_cast<int64_t>(srow) * ss +
+                       part * 8;
+  *reinterpret_cast<uint4*>(out) = make_uint4(E::pack(x.x * scale, x.y * scale), E::pack(x.z * scale, x.w * scale),
+                                              E::pack(y.x * scale, y.y * scale), E::pack(y.z * scale, y.w * scale));
+}
+
 // Launch order of the backward kernels (dalpha_kernel only with a relay scale).
 static const char* const kBwdKernelNames[] = {"delta_kernel", "keyglobal_kernel", "reduce_kernel", "dalpha_kernel",
-                                              "keylocal_kernel", "dq_kernel"};
+                                              "keylocal_kernel", "dq_kernel", "dq_convert_kernel"};
+
+// The key passes (and, unfused, the dQ pass; fused, the dQ conversion).
+template <int D, bool BF16, bool FUSED, typename Mark, typename Done>
+static cudaError_t launch_key_passes(BwdLaunch& L, cudaStream_t st, Mark& mark, Done& done) {
+  const QueryPassParams& qp = L.qp;
+  const int B = qp.B, H = qp.H, S = qp.S;
+  const int Spad = qp.n_qtiles * kTile;
+  cudaError_t e;
+  const KeyPassParams& gp = L.global;
+  const int Hkv = gp.H / gp.kv_groups;
+  const int n_gtiles = (gp.NG + kTile - 1) / kTile;
+  {
+    using C = KeyCfg<D, FUSED>;
+    auto kern = keyglobal_kernel<D, BF16, FUSED>;
+    if ((e = set_smem(kern, C::SMEM)) != cudaSuccess) return e;
+    if ((e = mark(1)) != cudaSuccess) return e;
+    kern<<<dim3(n_gtiles * gp.n_split, Hkv, B), 320, C::SMEM, st>>>(gp);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  {
+    const int64_t n4 = static_cast<int64_t>(B) * Hkv * gp.NG * D / 4;
+    const int64_t nb = (n4 + 255) / 256;
+    if ((e = mark(2)) != cudaSuccess) return e;
+    reduce_kernel<<<static_cast<int>(nb < 4096 ? nb : 4096), 256, 0, st>>>(
+        reinterpret_cast<const float4*>(gp.part_k), reinterpret_cast<const float4*>(gp.part_v), n4, gp.n_split,
+        reinterpret_cast<float4*>(L.dgk), reinterpret_cast<float4*>(L.dgv));
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  if (L.d_alpha && gp.R > 1) {
+    if ((e = mark(3)) != cudaSuccess) return e;
+    dalpha_kernel<BF16><<<Hkv, 256, 0, st>>>(L.dgk, L.dgv, L.gk_rows, L.gv_rows, B, Hkv, gp.NG, gp.R, D, L.d_alpha);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  const KeyPassParams& lp = L.local;
+  {
+    using C = KeyLocalCfg<D, FUSED>;
+    auto kern = keylocal_kernel<D, BF16, FUSED>;
+    if ((e = set_smem(kern, C::SMEM)) != cudaSuccess) return e;
+    const int n_tiles = lp.n_ktiles * Hkv * B;
+    if ((e = mark(4)) != cudaSuccess) return e;
+    kern<<<dim3(n_tiles < sm_count() ? n_tiles : sm_count()), C::THREADS, C::SMEM, st>>>(lp);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  if constexpr (FUSED) {
+    const int64_t n = static_cast<int64_t>(B) * H * S * (D / 8);
+    if ((e = mark(6)) != cudaSuccess) return e;
+    dq_convert_kernel<D, BF16><<<dim3(static_cast<unsigned>((n + 255) / 256)), 256, 0, st>>>(
+        gp.dq_acc, qp.out, qp.out_sb, qp.out_sh, qp.out_ss, static_cast<int64_t>(B) * H * S, H, S, Spad, qp.scale);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  } else {
+    auto kern = dq_kernel<D, BF16>;
+    if ((e = set_smem(kern, DqCfg<D>::SMEM)) != cudaSuccess) return e;
+    const int n_tiles = qp.n_qtiles * H * B;
+    if ((e = mark(5)) != cudaSuccess) return e;
+    kern<<<dim3(n_tiles < sm_count() ? n_tiles : sm_count()), DqCfg<D>::THREADS, DqCfg<D>::SMEM, st>>>(qp);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  return done();
+}
 
 template <int D, bool BF16>
 static cudaError_t launch_bwd_t(const BwdLaunch& L_, cudaStream_t st) {
@@ -1315,52 +1507,14 @@ static cudaError_t launch_bwd_t(const BwdLaunch& L_, cudaStream_t st) {
     dim3 grid((Spad + RPB - 1) / RPB, B * H);
     if ((e = mark(0)) != cudaSuccess) return e;
     delta_kernel<D, BF16><<<grid, 256, 0, st>>>(L.o, L.d_o, L.o_st[0], L.o_st[1], L.o_st[2], L.do_st[0], L.do_st[1],
-                                                L.do_st[2], L.lse_in, H, S, Spad, L.lse2, L.delta);
+                                                L.do_st[2], L.lse_in, H, S, Spad, L.lse2, L.delta,
+                                                L.fused ? L.global.dq_acc : nullptr);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
-  const KeyPassParams& gp = L.global;
-  const int Hkv = gp.H / gp.kv_groups;
-  const int n_gtiles = (gp.NG + kTile - 1) / kTile;
-  {
-    auto kern = keyglobal_kernel<D, BF16>;
-    if ((e = set_smem(kern, KeyCfg<D>::SMEM)) != cudaSuccess) return e;
-    if ((e = mark(1)) != cudaSuccess) return e;
-    kern<<<dim3(n_gtiles * gp.n_split, Hkv, B), 320, KeyCfg<D>::SMEM, st>>>(gp);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if constexpr (D == 128) {
+    if (L.fused) return launch_key_passes<D, BF16, true>(L, st, mark, done);
   }
-  {
-    const int64_t n4 = static_cast<int64_t>(B) * Hkv * gp.NG * D / 4;
-    const int64_t nb = (n4 + 255) / 256;
-    if ((e = mark(2)) != cudaSuccess) return e;
-    reduce_kernel<<<static_cast<int>(nb < 4096 ? nb : 4096), 256, 0, st>>>(
-        reinterpret_cast<const float4*>(gp.part_k), reinterpret_cast<const float4*>(gp.part_v), n4, gp.n_split,
-        reinterpret_cast<float4*>(L.dgk), reinterpret_cast<float4*>(L.dgv));
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  }
-  if (L.d_alpha && gp.R > 1) {
-    if ((e = mark(3)) != cudaSuccess) return e;
-    dalpha_kernel<BF16><<<Hkv, 256, 0, st>>>(L.dgk, L.dgv, L.gk_rows, L.gv_rows, B, Hkv, gp.NG, gp.R, D, L.d_alpha);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  }
-  const KeyPassParams& lp = L.local;
-  {
-    auto kern = keylocal_kernel<D, BF16>;
-    if ((e = set_smem(kern, KeyLocalCfg<D>::SMEM)) != cudaSuccess) return e;
-    const int n_tiles = lp.n_ktiles * Hkv * B;
-    if ((e = mark(4)) != cudaSuccess) return e;
-    kern<<<dim3(n_tiles < sm_count() ? n_tiles : sm_count()), KeyLocalCfg<D>::THREADS, KeyLocalCfg<D>::SMEM, st>>>(
-        lp);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  }
-  {
-    auto kern = dq_kernel<D, BF16>;
-    if ((e = set_smem(kern, DqCfg<D>::SMEM)) != cudaSuccess) return e;
-    const int n_tiles = qp.n_qtiles * H * B;
-    if ((e = mark(5)) != cudaSuccess) return e;
-    kern<<<dim3(n_tiles < sm_count() ? n_tiles : sm_count()), DqCfg<D>::THREADS, DqCfg<D>::SMEM, st>>>(qp);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  }
-  return done();
+  return launch_key_passes<D, BF16, false>(L, st, mark, done);
 }
 
 const char* bwd_kernel_name(int id) {

@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <climits>
 #include <cmath>
 #include <cstdarg>
@@ -141,9 +142,12 @@ int rows_per_block(int use_relay, int top_k) { return use_relay ? 1 + top_k : 1;
 //   lse2, delta  [B, H, Spad]              Spad = 128 * ceil(S / 128)
 //   dgk, dgv     [B, Hkv, NG, D]           reduced global-row gradients
 //   part_k/v     [n_split, B, Hkv, NG, D]  per-split partials
+//   dq_acc       [B, H, Spad, D]           fused backward only (head_dim 128)
 struct BwdLayout {
   int n_split;
-  size_t off_lse2, off_delta, off_dgk, off_dgv, off_pk, off_pv, total;
+  size_t off_lse2, off_delta, off_dgk, off_dgv, off_pk, off_pv, off_dqacc;
+  size_t total;        // cra_bwd: no dQ accumulator
+  size_t total_fused;  // cra_bwd_fused: adds the fp32 dQ accumulator when head_dim = 128
 };
 
 size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -174,7 +178,9 @@ BwdLayout bwd_layout(int batch, int heads, int kv_heads, int seq_len, int head_d
   L.off_dgv = L.off_dgk + gsz;
   L.off_pk = L.off_dgv + gsz;
   L.off_pv = L.off_pk + gsz * L.n_split;
-  L.total = L.off_pv + gsz * L.n_split;
+  L.off_dqacc = L.off_pv + gsz * L.n_split;
+  L.total = L.off_dqacc;
+  L.total_fused = L.off_dqacc + (head_dim == 128 ? round256(sizeof(float) * batch * heads * Spad * head_dim) : 0);
   return L;
 }
 
@@ -318,7 +324,8 @@ int bwd_impl(const void* q, const void* k, const void* v, const void* o, const v
              float softmax_scale, const float* relay_log_scale, void* dq, void* dk, void* dv,
              const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
              float* d_relay_log_scale, void* workspace, size_t workspace_bytes, int* dev_error, void* stream,
-             cudaEvent_t* events, int* n_kernels, int* kernel_ids) {
+             cudaEvent_t* events, int* n_kernels, int* kernel_ids, int fused_req) {
+  const bool fused = fused_req && head_dim == 128;
   CRA_TRY(check_common(batch, heads, kv_heads, seq_len, head_dim, dtype, top_k));
   CRA_TRY(check_tensor("q", q, q_strides, batch, heads));
   CRA_TRY(check_tensor("k", k, k_strides, batch, kv_heads));
@@ -334,8 +341,9 @@ int bwd_impl(const void* q, const void* k, const void* v, const void* o, const v
   if (!(softmax_scale > 0.f) || !std::isfinite(softmax_scale))
     return fail(CRA_ERR_INVALID_ARGUMENT, "softmax_scale must be finite and > 0");
   const BwdLayout lay = bwd_layout(batch, heads, kv_heads, seq_len, head_dim, use_relay, top_k);
-  if (!workspace || workspace_bytes < lay.total)
-    return fail(CRA_ERR_WORKSPACE, "workspace: %zu bytes given, %zu needed", workspace_bytes, lay.total);
+  const size_t need = fused ? lay.total_fused : lay.total;
+  if (!workspace || workspace_bytes < need)
+    return fail(CRA_ERR_WORKSPACE, "workspace: %zu bytes given, %zu needed", workspace_bytes, need);
   if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
     return fail(CRA_ERR_MISALIGNED, "workspace: base not 256-byte aligned");
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -410,6 +418,7 @@ int bwd_impl(const void* q, const void* k, const void* v, const void* o, const v
     kp.relay_scale = use_relay ? relay_log_scale : nullptr;
     kp.part_k = reinterpret_cast<float*>(ws + lay.off_pk);
     kp.part_v = reinterpret_cast<float*>(ws + lay.off_pv);
+    kp.dq_acc = fused ? reinterpret_cast<float*>(ws + lay.off_dqacc) : nullptr;
     kp.B = batch;
     kp.H = heads;
     kp.kv_groups = heads / kv_heads;
@@ -445,6 +454,7 @@ int bwd_impl(const void* q, const void* k, const void* v, const void* o, const v
     if (me != cudaSuccess) return fail(CRA_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(me));
   }
   L.events = events;
+  L.fused = fused;
   cudaError_t e = launch_bwd(L, head_dim, bf16, st);
   if (n_kernels) *n_kernels = L.n_kernels;
   if (kernel_ids)
@@ -466,7 +476,26 @@ int cra_bwd(const void* q, const void* k, const void* v, const void* o, const vo
   return bwd_impl(q, k, v, o, d_o, lse, g_k, g_v, g_src, q_strides, k_strides, v_strides, o_strides, do_strides,
                   batch, heads, kv_heads, seq_len, head_dim, dtype, use_relay, top_k, softmax_scale, relay_log_scale,
                   dq, dk, dv, dq_strides, dk_strides, dv_strides, d_relay_log_scale, workspace, workspace_bytes,
-                  dev_error, stream, nullptr, nullptr, nullptr);
+                  dev_error, stream, nullptr, nullptr, nullptr, 0);
+}
+
+int cra_bwd_fused(const void* q, const void* k, const void* v, const void* o, const void* d_o, const float* lse,
+                  const void* g_k, const void* g_v, const int32_t* g_src, const int64_t* q_strides,
+                  const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                  const int64_t* do_strides, int batch, int heads, int kv_heads, int seq_len, int head_dim, int dtype,
+                  int use_relay, int top_k, float softmax_scale, const float* relay_log_scale, void* dq, void* dk,
+                  void* dv, const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
+                  float* d_relay_log_scale, void* workspace, size_t workspace_bytes, int* dev_error, void* stream) {
+  return bwd_impl(q, k, v, o, d_o, lse, g_k, g_v, g_src, q_strides, k_strides, v_strides, o_strides, do_strides,
+                  batch, heads, kv_heads, seq_len, head_dim, dtype, use_relay, top_k, softmax_scale, relay_log_scale,
+                  dq, dk, dv, dq_strides, dk_strides, dv_strides, d_relay_log_scale, workspace, workspace_bytes,
+                  dev_error, stream, nullptr, nullptr, nullptr, 1);
+}
+
+size_t cra_bwd_fused_workspace_bytes(int batch, int heads, int kv_heads, int seq_len, int head_dim, int use_relay,
+                                     int top_k) {
+  if (check_common(batch, heads, kv_heads, seq_len, head_dim, CRA_BF16, top_k) != CRA_OK) return 0;
+  return bwd_layout(batch, heads, kv_heads, seq_len, head_dim, use_relay, top_k).total_fused;
 }
 
 int cra_bwd_kernel_times(const void* q, const void* k, const void* v, const void* o, const void* d_o,
@@ -477,7 +506,7 @@ int cra_bwd_kernel_times(const void* q, const void* k, const void* v, const void
                          const float* relay_log_scale, void* dq, void* dk, void* dv, const int64_t* dq_strides,
                          const int64_t* dk_strides, const int64_t* dv_strides, float* d_relay_log_scale,
                          void* workspace, size_t workspace_bytes, int* dev_error, void* stream, float* kernel_ms,
-                         const char** kernel_names, int max_kernels, int* n_kernels) {
+                         const char** kernel_names, int max_kernels, int* n_kernels, int fused) {
   if (!kernel_ms || !n_kernels) return fail(CRA_ERR_INVALID_ARGUMENT, "kernel_ms / n_kernels: null pointer");
   CRA_TRY(bind_context());
   cudaEvent_t ev[BwdLaunch::kMaxKernels + 1];
@@ -492,7 +521,7 @@ int cra_bwd_kernel_times(const void* q, const void* k, const void* v, const void
     status = bwd_impl(q, k, v, o, d_o, lse, g_k, g_v, g_src, q_strides, k_strides, v_strides, o_strides, do_strides,
                       batch, heads, kv_heads, seq_len, head_dim, dtype, use_relay, top_k, softmax_scale,
                       relay_log_scale, dq, dk, dv, dq_strides, dk_strides, dv_strides, d_relay_log_scale, workspace,
-                      workspace_bytes, dev_error, stream, ev, &n, ids);
+                      workspace_bytes, dev_error, stream, ev, &n, ids, fused);
   if (status == CRA_OK) {
     e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) status = fail(CRA_ERR_CUDA, "cudaStreamSynchronize: %s", cudaGetErrorString(e));
@@ -534,14 +563,31 @@ int cra_relay_build_shard(const void* k, const void* v, const int64_t* k_strides
 int cra_fwd_shard(const void* q, const void* k, const void* v, const void* g_k, const void* g_v,
                   const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, int batch, int heads,
                   int kv_heads, int64_t seq_len, int64_t q_begin, int q_len, int64_t kv_begin, int kv_len,
-                  int head_dim, int dtype, int use_relay, int top_k, float softmax_scale, void* o,
-                  const int64_t* o_strides, float* lse, int* dev_error, void* stream) {
+                  const void* k_edge, const void* v_edge, const int64_t* ke_strides, const int64_t* ve_strides,
+                  int64_t edge_begin, int edge_len, int head_dim, int dtype, int use_relay, int top_k,
+                  float softmax_scale, void* o, const int64_t* o_strides, float* lse, int* dev_error, void* stream) {
   CRA_TRY(check_common(batch, heads, kv_heads, q_len, head_dim, dtype, top_k));
   if (seq_len < 1 || seq_len > INT32_MAX) return fail(CRA_ERR_INVALID_ARGUMENT, "seq_len out of range");
   const int W = cra_window(seq_len);
   if (q_begin < 0 || q_begin + q_len > seq_len) return fail(CRA_ERR_INVALID_ARGUMENT, "query shard outside the sequence");
-  if (kv_begin < 0 || kv_len < 1 || kv_begin > q_begin - (W - 1) && kv_begin > 0)
+  const bool edge = k_edge != nullptr || v_edge != nullptr;
+  if (edge) {
+    if (!k_edge || !v_edge) return fail(CRA_ERR_INVALID_ARGUMENT, "k_edge / v_edge: give both or neither");
+    if (kv_begin != q_begin) return fail(CRA_ERR_INVALID_ARGUMENT, "with an edge copy K/V rows start at q_begin");
+    const int64_t need_lo = q_begin - (W - 1) > 0 ? q_begin - (W - 1) : 0;
+    const int64_t need_hi = std::min<int64_t>(q_begin + W + 255, q_begin + q_len);
+    if (edge_begin < 0 || edge_begin > need_lo || edge_begin + edge_len < need_hi)
+      return fail(CRA_ERR_INVALID_ARGUMENT,
+                  "edge rows [%lld, %lld) must cover [max(q_begin - (W - 1), 0), min(q_begin + W + 255, q_begin + "
+                  "q_len)) = "
+                  "[%lld, %lld)",
+                  static_cast<long long>(edge_begin), static_cast<long long>(edge_begin + edge_len),
+                  static_cast<long long>(need_lo), static_cast<long long>(need_hi));
+    CRA_TRY(check_tensor("k_edge", k_edge, ke_strides, batch, kv_heads));
+    CRA_TRY(check_tensor("v_edge", v_edge, ve_strides, batch, kv_heads));
+  } else if (kv_begin < 0 || kv_len < 1 || kv_begin > q_begin - (W - 1) && kv_begin > 0) {
     return fail(CRA_ERR_INVALID_ARGUMENT, "K/V rows must start at or before q_begin - (W - 1) (the local window)");
+  }
   if (kv_begin + kv_len < q_begin + q_len)
     return fail(CRA_ERR_INVALID_ARGUMENT, "K/V rows must reach the last query of the shard");
   CRA_TRY(check_tensor("q", q, q_strides, batch, heads));
@@ -565,6 +611,12 @@ int cra_fwd_shard(const void* q, const void* k, const void* v, const void* g_k, 
   CRA_TRY(make_tmap("v", &p.tm_v, v, bf16, head_dim, kv_len, kv_heads, batch, v_strides));
   CRA_TRY(make_tmap("g_k", &p.tm_gk, g_k, bf16, head_dim, NG, kv_heads, batch, g_st));
   CRA_TRY(make_tmap("g_v", &p.tm_gv, g_v, bf16, head_dim, NG, kv_heads, batch, g_st));
+  if (edge) {
+    CRA_TRY(make_tmap("k_edge", &p.tm_ke, k_edge, bf16, head_dim, edge_len, kv_heads, batch, ke_strides));
+    CRA_TRY(make_tmap("v_edge", &p.tm_ve, v_edge, bf16, head_dim, edge_len, kv_heads, batch, ve_strides));
+    p.has_edge = 1;
+    p.edge_begin = static_cast<int>(edge_begin);
+  }
   p.tm_do = p.tm_q;
   p.out = o;
   p.out_sb = o_strides[0];

@@ -28,8 +28,10 @@
 // P, and the commit that signals "scores ready" also covers every earlier PV
 // product: when the softmax sees S_x(n), O_x holds all of P_x V up to n - 1.
 // A CTA may also work on one GPU's shard of a sequence split across GPUs:
-// queries [q_begin, q_begin + q_len) with K / V rows from kv_begin (a W - 1
-// row halo before the shard) and the full global-row list.
+// queries [q_begin, q_begin + q_len) with K / V rows from kv_begin and the
+// full global-row list; the pairs whose window reaches below kv_begin read
+// their band from a small edge copy (halo rows of the previous shard + the
+// shard's first rows) instead.
 // While one softmax warpgroup works on its scores the tensor core computes
 // the other tile's scores and the PV products (ping-pong).
 #include "geom.cuh"
@@ -138,6 +140,13 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
         for (int c = 0; c < D / 64; ++c)
           tma_load_4d(sbase + C::OFF_Q + x * C::TB + c * kTile * 128, &p.tm_q, BAR(C::B_QFULL), c * 64,
                       m0 + x * kTile - p.q_begin, h, b);
+      // band keys of this pair from the edge copy when its window reaches
+      // below this shard's own K / V rows
+      const bool use_edge = p.has_edge && local_start(m0, W) < p.kv_begin;
+      if (p.has_edge) {
+        tma_prefetch(&p.tm_ke);
+        tma_prefetch(&p.tm_ve);
+      }
       int issued = 0;
       for (int i = 0; i < nload; ++i) {
         const int sl = i % C::NSLOT;
@@ -146,11 +155,12 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
         bool g, ua, ub;
         sch.tile(i >> 1, row0, g, ua, ub);
         const bool is_v = i & 1;
-        const CUtensorMap* m = g ? (is_v ? &p.tm_gv : &p.tm_gk) : (is_v ? &p.tm_v : &p.tm_k);
+        const CUtensorMap* m = g ? (is_v ? &p.tm_gv : &p.tm_gk)
+                                 : use_edge ? (is_v ? &p.tm_ve : &p.tm_ke) : (is_v ? &p.tm_v : &p.tm_k);
         mbar_expect_tx(BAR(C::B_FULL + sl), C::TB);
         for (int c = 0; c < D / 64; ++c)
           tma_load_4d(sbase + C::OFF_RING + sl * C::TB + c * kTile * 128, m, BAR(C::B_FULL + sl), c * 64,
-                      g ? row0 : row0 - p.kv_begin, hk, b);
+                      g ? row0 : row0 - (use_edge ? p.edge_begin : p.kv_begin), hk, b);
         ++issued;
       }
       // Do not leave while copies into this CTA's shared memory are in

@@ -15,6 +15,13 @@ struct alignas(64) QueryPassParams {
   CUtensorMap tm_gk;  // [B, Hkv, NG, D]
   CUtensorMap tm_gv;  // [B, Hkv, NG, D]
   CUtensorMap tm_do;  // [B, H,   S,  D]   (backward only)
+  // Sequence shard with an edge copy (forward): pairs whose local window
+  // starts before kv_begin read their band keys from tm_ke / tm_ve, whose
+  // row 0 is absolute position edge_begin (the previous shard's last W - 1
+  // rows followed by this shard's first rows).
+  CUtensorMap tm_ke;
+  CUtensorMap tm_ve;
+  int has_edge, edge_begin;
   void* out;          // forward: O;  backward: dQ  (element strides below)
   int64_t out_sb, out_sh, out_ss;
   int out_v8;         // every output row starts on a 32-byte boundary: 32-byte stores allowed
@@ -49,6 +56,9 @@ struct alignas(64) KeyPassParams {
   const float* relay_scale;// [Hkv] relay_log_scale (alpha) per kv head, or null
   // global mode: fp32 partial outputs [n_split, B, Hkv, NG, D]
   float* part_k; float* part_v;
+  // fused backward: fp32 dQ accumulator [B, H, Spad, D] (unscaled), zeroed
+  // by the delta kernel; the key passes add dS K into it
+  float* dq_acc;
   int B, H, kv_groups, S, W, R, NB, NG, top_k;
   int n_ktiles;       // key tiles per (b, hkv)
   int n_split;        // global mode: query splits per key tile
@@ -74,6 +84,7 @@ struct BwdLaunch {
   const void* gv_rows;
   // Optional timing: when non-null, events[i] is recorded on the stream just
   // before kernel i and events[n_kernels] after the last one.
+  bool fused;              // dQ from the key passes (fp32 atomics), no dQ pass
   static constexpr int kMaxKernels = 8;
   cudaEvent_t* events;
   int n_kernels;                // set by launch_bwd: kernels launched (timed)

@@ -106,10 +106,18 @@ int cra_fwd(const void* q, const void* k, const void* v, const void* g_k, const 
  * The full list is the concatenation over shards in order (an all-gather).
  *
  * cra_fwd_shard: forward for the shard's queries.  q / o / lse hold q_len
- * rows (lse contiguous [batch, heads, q_len]); k / v hold kv_len rows
- * starting at absolute position kv_begin <= max(q_begin - (W - 1), 0) (the
- * local-window halo from the previous shard); g_k / g_v are the FULL global
- * list of the sequence.  Same numerics as cra_fwd on the whole sequence.
+ * rows (lse contiguous [batch, heads, q_len]); g_k / g_v are the FULL global
+ * list of the sequence.  K / V, either way:
+ *   - without an edge copy (k_edge = v_edge = NULL): k / v hold kv_len rows
+ *     starting at absolute position kv_begin <= max(q_begin - (W - 1), 0),
+ *     i.e. the local-window halo from the previous shard in front;
+ *   - with an edge copy: k / v are the shard's own rows (kv_begin = q_begin)
+ *     and k_edge / v_edge hold edge_len rows from absolute position
+ *     edge_begin, covering [max(q_begin - (W - 1), 0), min(q_begin + W + 255,
+ *     q_begin + q_len)): the halo plus the shard's first rows, a few thousand rows
+ *     in all, read by the query tiles whose window reaches into the halo.
+ *     No copy of the whole shard is needed.
+ * Same numerics as cra_fwd on the whole sequence.
  * Replaces nothing in the reference (single-GPU only there); used for the
  * sequence-split configuration. */
 int cra_relay_build_shard(const void* k, const void* v, const int64_t* k_strides, const int64_t* v_strides,
@@ -119,8 +127,9 @@ int cra_relay_build_shard(const void* k, const void* v, const int64_t* k_strides
 int cra_fwd_shard(const void* q, const void* k, const void* v, const void* g_k, const void* g_v,
                   const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, int batch, int heads,
                   int kv_heads, int64_t seq_len, int64_t q_begin, int q_len, int64_t kv_begin, int kv_len,
-                  int head_dim, int dtype, int use_relay, int top_k, float softmax_scale, void* o,
-                  const int64_t* o_strides, float* lse, int* dev_error, void* stream);
+                  const void* k_edge, const void* v_edge, const int64_t* ke_strides, const int64_t* ve_strides,
+                  int64_t edge_begin, int edge_len, int head_dim, int dtype, int use_relay, int top_k,
+                  float softmax_scale, void* o, const int64_t* o_strides, float* lse, int* dev_error, void* stream);
 
 /* Bytes of device workspace cra_bwd needs for these sizes (256-byte aligned
  * base required). */
@@ -133,7 +142,7 @@ size_t cra_bwd_workspace_bytes(int batch, int heads, int kv_heads, int seq_len, 
  * exp(relay_log_scale[h]) on the way (chain rule through the scaled rows),
  * and d_relay_log_scale (fp32 [kv_heads], overwritten) receives
  * sum(dG_k * G_k + dG_v * G_v) over the relay rows.
- * Deterministic: no floating-point atomics.
+ * Deterministic: no floating-point atomics; every sum has a fixed order.
  * Replaces CronRootAttentionV14Function.backward, core.py:3626-3759, with its
  * kernels core.py:1165-1316 (dQ), 1650-1745 (local dK/dV), 1755-1889
  * (strided dK/dV), 2381-2492 (relay dK/dV), 2767-2815 (relay scatter). */
@@ -145,12 +154,35 @@ int cra_bwd(const void* q, const void* k, const void* v, const void* o, const vo
             const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
             float* d_relay_log_scale, void* workspace, size_t workspace_bytes, int* dev_error, void* stream);
 
+/* Backward variant that computes dQ inside the two key-centric passes (a
+ * fifth GEMM per 128 x 64 block, dQ^T = K^T dS^T, added into an fp32
+ * accumulator in the workspace with atomic adds, then converted), so the
+ * scores are recomputed once instead of twice and there is no dQ pass.  dq
+ * may differ in the last bits between calls (atomic order); dk, dv are
+ * summed in a fixed order.  Same arguments as cra_bwd, with a workspace of
+ * cra_bwd_fused_workspace_bytes(); head_dim 64 runs cra_bwd's kernels.
+ * Measured on B200 at B1 H16 S64K D128 it is slower than cra_bwd (the
+ * accumulator traffic and the longer per-unit chain cost more than the dQ
+ * pass saves), so the Python API uses cra_bwd.  No counterpart in the
+ * reference beyond the backward it shares with cra_bwd. */
+int cra_bwd_fused(const void* q, const void* k, const void* v, const void* o, const void* d_o, const float* lse,
+                  const void* g_k, const void* g_v, const int32_t* g_src, const int64_t* q_strides,
+                  const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                  const int64_t* do_strides, int batch, int heads, int kv_heads, int seq_len, int head_dim, int dtype,
+                  int use_relay, int top_k, float softmax_scale, const float* relay_log_scale, void* dq, void* dk,
+                  void* dv, const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
+                  float* d_relay_log_scale, void* workspace, size_t workspace_bytes, int* dev_error, void* stream);
+size_t cra_bwd_fused_workspace_bytes(int batch, int heads, int kv_heads, int seq_len, int head_dim, int use_relay,
+                                     int top_k);
+
 /* Measurement helper (no counterpart in the reference): runs cra_bwd with the
  * same arguments, records a CUDA event on `stream` before each of its kernels
  * and after the last, SYNCHRONIZES the stream, and returns each kernel's
  * event-to-event time in kernel_ms[i] (ms) and its name in kernel_names[i]
  * (static strings; may be NULL) for i < *n_kernels <= max_kernels, in launch
- * order.  For benchmarks and profiles only. */
+ * order; fused != 0 times cra_bwd_fused's kernels instead (workspace of
+ * cra_bwd_fused_workspace_bytes()).
+ * For benchmarks and profiles only. */
 int cra_bwd_kernel_times(const void* q, const void* k, const void* v, const void* o, const void* d_o,
                          const float* lse, const void* g_k, const void* g_v, const int32_t* g_src,
                          const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
@@ -159,7 +191,7 @@ int cra_bwd_kernel_times(const void* q, const void* k, const void* v, const void
                          const float* relay_log_scale, void* dq, void* dk, void* dv, const int64_t* dq_strides,
                          const int64_t* dk_strides, const int64_t* dv_strides, float* d_relay_log_scale,
                          void* workspace, size_t workspace_bytes, int* dev_error, void* stream, float* kernel_ms,
-                         const char** kernel_names, int max_kernels, int* n_kernels);
+                         const char** kernel_names, int max_kernels, int* n_kernels, int fused);
 
 /* Backward without a caller-provided workspace, for callers that cannot
  * allocate device memory (no access to an allocator, or code that must not

@@ -29,7 +29,12 @@ class OracleShardOps:
                 out_v.append(torch.gather(v, 2, i.view(B, H, 1, 1).expand(B, H, 1, D)))
         return torch.cat(out_k, 2), torch.cat(out_v, 2)
 
-    def forward_shard(self, q, k, v, gk, gv, seq_len, q_begin, kv_begin, use_relay, top_k):
+    def forward_shard(self, q, k, v, gk, gv, seq_len, q_begin, kv_begin, use_relay, top_k, edge=None):
+        if edge is not None:  # halo rows from the edge copy in front of the shard's own rows
+            ke, ve, e0 = edge
+            k = torch.cat([ke[:, :, :kv_begin - e0], k], 2)
+            v = torch.cat([ve[:, :, :kv_begin - e0], v], 2)
+            kv_begin = e0
         B, H, n, D = q.shape
         W = O.window(seq_len)
         R = 1 + top_k if use_relay else 1

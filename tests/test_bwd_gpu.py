@@ -97,3 +97,43 @@ def test_config3_full_size(cuda_device):
         assert _r["ok"], _r
         for name, x, y in (("dq", sl(dq), rdq), ("dk", sl(dk), rdk), ("dv", sl(dv), rdv)):
             assert rel_l2(x, y) <= GRAD_REL_L2, (name, rel_l2(x, y))
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,S,dt,seed", [(2, 2, 2, 4100, torch.bfloat16, 7), (1, 4, 2, 2500, torch.float16, 5),
+                                               (1, 2, 2, 300, torch.bfloat16, 3)])
+def test_fused_backward_through_c_abi(B, Hq, Hkv, S, dt, seed, cuda_device):
+    """cra_bwd_fused (dQ from the key passes by atomic adds) against the
+    oracle, and dk / dv bit for bit equal to cra_bwd's."""
+    import ctypes
+    import cron_root_attention as cra
+    from cron_root_attention import _lib
+    L = _lib.lib()
+    dev = cuda_device
+    D = 128
+    q, k, v, do = inputs(B, Hq, Hkv, S, D, dt, seed, with_do=True)
+    qd, kd, vd, dod = (t.to(dev) for t in (q, k, v, do))
+    qd.requires_grad_(True), kd.requires_grad_(True), vd.requires_grad_(True)
+    o = cra.cron_root_attention(qd, kd, vd, kv_groups=Hq // Hkv)
+    o.backward(dod, retain_graph=True)
+    ctx = o.grad_fn
+    qc, kc, vc, oc, lse, gk, gv, gsrc, _ = ctx.saved_tensors
+    st = _lib.strides3
+    use_relay = int(S > 2048)
+    outs = [torch.empty_like(t) for t in (qc, kc, vc)]
+    ws_b = L.cra_bwd_fused_workspace_bytes(B, Hq, Hkv, S, D, use_relay, 2)
+    assert ws_b > L.cra_bwd_workspace_bytes(B, Hq, Hkv, S, D, use_relay, 2)
+    ws = torch.empty(ws_b, device=dev, dtype=torch.uint8)
+    s = torch.cuda.current_stream(dev).cuda_stream
+    _lib.check(L.cra_bwd_fused(qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), oc.data_ptr(), dod.data_ptr(),
+                               lse.data_ptr(), gk.data_ptr(), gv.data_ptr(), gsrc.data_ptr(), st(qc), st(kc), st(vc),
+                               st(oc), st(dod), B, Hq, Hkv, S, D, 1 if dt == torch.bfloat16 else 0, use_relay, 2,
+                               ctypes.c_float(D ** -0.5), None, outs[0].data_ptr(), outs[1].data_ptr(),
+                               outs[2].data_ptr(), st(outs[0]), st(outs[1]), st(outs[2]), None, ws.data_ptr(), ws_b,
+                               None, s), "cra_bwd_fused")
+    torch.cuda.synchronize(dev)
+    assert cra.check_device_errors(dev) == 0
+    _, rdq, rdk, rdv, _ = O.forward_backward(q, k, v, do, kv_groups=Hq // Hkv)
+    for name, x, y in (("dq", outs[0], rdq), ("dk", outs[1], rdk), ("dv", outs[2], rdv)):
+        assert rel_l2(x, y) <= GRAD_REL_L2, (name, rel_l2(x, y))
+    assert torch.equal(outs[1], kd.grad) and torch.equal(outs[2], vd.grad)
+    assert rel_l2(outs[0], qd.grad) <= 1e-3

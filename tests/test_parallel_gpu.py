@@ -15,7 +15,11 @@ from parity import fwd_check, inputs
 pytestmark = pytest.mark.gpu
 
 
-def _emulate(q, k, v, S, world, dev):
+def _emulate(q, k, v, S, world, dev, edge=True):
+    """Every shard of a world-way split run on this GPU.  edge=True: each
+    shard reads its own K / V rows in place plus a small edge copy (halo +
+    first W + 256 rows), as the multi-GPU path does; edge=False: the halo
+    rows placed in front of a copy of the shard."""
     from cron_root_attention.parallel import LibcraShardOps, seq_shard, window
     ops = LibcraShardOps()
     W = window(S)
@@ -29,17 +33,26 @@ def _emulate(q, k, v, S, world, dev):
     gk, gv = torch.cat(gks, 2).contiguous(), torch.cat(gvs, 2).contiguous()
     for b, e in bounds:
         kb = max(0, b - (W - 1))
-        outs.append(ops.forward_shard(q[:, :, b:e].contiguous(), k[:, :, kb:e].contiguous(),
-                                      v[:, :, kb:e].contiguous(), gk, gv, S, b, kb, use_relay, 2))
+        if edge and b > 0:
+            x = min(b + W + 256, e)
+            eg = (k[:, :, kb:x].contiguous(), v[:, :, kb:x].contiguous(), kb)
+            outs.append(ops.forward_shard(q[:, :, b:e].contiguous(), k[:, :, b:e].contiguous(),
+                                          v[:, :, b:e].contiguous(), gk, gv, S, b, b, use_relay, 2, edge=eg))
+        else:
+            outs.append(ops.forward_shard(q[:, :, b:e].contiguous(), k[:, :, kb:e].contiguous(),
+                                          v[:, :, kb:e].contiguous(), gk, gv, S, b, kb, use_relay, 2))
     torch.cuda.synchronize(dev)
     return torch.cat(outs, 2)
 
 
-@pytest.mark.parametrize("S,world,D,dt", [(5000, 2, 128, torch.bfloat16), (9000, 3, 64, torch.float16),
-                                          (40000, 8, 128, torch.bfloat16)])
-def test_sequence_split_emulated_on_one_gpu(S, world, D, dt, cuda_device):
+@pytest.mark.parametrize("S,world,D,dt,edge", [(5000, 2, 128, torch.bfloat16, True),
+                                               (5000, 2, 128, torch.bfloat16, False),
+                                               (9000, 3, 64, torch.float16, True),
+                                               (40000, 8, 128, torch.bfloat16, True),
+                                               (40000, 8, 128, torch.bfloat16, False)])
+def test_sequence_split_emulated_on_one_gpu(S, world, D, dt, edge, cuda_device):
     q, k, v = inputs(1, 2, 2, S, D, dt, 50 + world)
-    o = _emulate(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), S, world, cuda_device)
+    o = _emulate(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), S, world, cuda_device, edge)
     ref, _ = O.forward(q, k, v)
     r = fwd_check(o, ref, dt)
     assert r["ok"], r
