@@ -39,6 +39,14 @@ _SIGNATURES = {
     "cra_fwd_shard": (_i, [_vp, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _i, _i, _i, ctypes.c_int64, ctypes.c_int64,
                            _i, ctypes.c_int64, _i, _vp, _vp, _i64p, _i64p, ctypes.c_int64, _i,
                            _i, _i, _i, _i, _f, _vp, _i64p, _vp, _vp, _vp]),
+    "cra_varlen_table_bytes": (ctypes.c_size_t, [_i]),
+    "cra_varlen_global_rows": (ctypes.c_int64, [_i64p, _i, _i]),
+    "cra_varlen_blocks": (ctypes.c_int64, [_i64p, _i]),
+    "cra_varlen_plan": (_i, [_i64p, _i, _i, _vp, _vp]),
+    "cra_relay_build_varlen": (_i, [_vp, _vp, _i64p, _i64p, _i, _i, _i64p, _i, _vp, _i, _i, _i, _vp, _vp, _vp, _vp,
+                                    _vp]),
+    "cra_fwd_varlen": (_i, [_vp, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _i, _i, _i, _i64p, _i, _vp, _i, _i, _i, _f,
+                            _vp, _i64p, _vp, _vp, _vp]),
     "cra_bwd_workspace_bytes": (ctypes.c_size_t, [_i, _i, _i, _i, _i, _i, _i]),
     "cra_bwd_fused_workspace_bytes": (ctypes.c_size_t, [_i, _i, _i, _i, _i, _i, _i]),
     "cra_bwd": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _i64p, _i64p,

@@ -260,16 +260,142 @@ def cron_root_attention_v14(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
 cron_root_attention = cron_root_attention_v14
 
 
+class _VarlenFunction(torch.autograd.Function):
+    """Packed variable-length attention.  Forward: one relay-build launch and
+    one attention launch for all documents (libcra's varlen entry points,
+    driven by a device document table).  Backward: the documents are grouped
+    by length and each group runs as one batched cra_bwd call (the global
+    rows rebuilt from K, which gives the same rows the forward used)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, seqs, kv_groups, relay_log_scale, relay_top_k):
+        if not (q.is_cuda and k.is_cuda and v.is_cuda):
+            raise RuntimeError("cron_root_attention: tensors must be on a CUDA device (no CPU fallback)")
+        B, Hq, T, D = q.shape
+        Hkv = k.shape[1]
+        if Hkv * kv_groups != Hq:
+            raise ValueError(f"kv_groups={kv_groups} inconsistent with H_q={Hq}, H_kv={Hkv}")
+        if not 1 <= relay_top_k <= 4:
+            raise ValueError("relay_top_k must be in 1..4")
+        dev = q.device
+        in_dtype = q.dtype
+        cdt = in_dtype if in_dtype in (torch.float16, torch.bfloat16) else torch.bfloat16
+        Dp = _padded_dim(D)
+        scale = 1.0 / math.sqrt(D)
+        L = lib()
+        qc, kc, vc = (_prep(t, cdt, Dp) for t in (q, k, v))
+        nd = len(seqs) - 1
+        cu = (ctypes.c_int64 * len(seqs))(*seqs)
+        NG = L.cra_varlen_global_rows(cu, nd, relay_top_k)
+        NBt = L.cra_varlen_blocks(cu, nd)
+        table = torch.empty(max(L.cra_varlen_table_bytes(nd), 1), device=dev, dtype=torch.uint8)
+        gk = torch.empty(B, Hkv, max(NG, 1), Dp, device=dev, dtype=cdt)
+        gv = torch.empty_like(gk)
+        gsrc = torch.empty(B, Hkv, max(NBt, 1), relay_top_k, device=dev, dtype=torch.int32)
+        alpha = None
+        if relay_log_scale is not None:
+            alpha = relay_log_scale.detach().to(device=dev, dtype=torch.float32).contiguous()
+            if alpha.numel() != Hkv:
+                raise ValueError("relay_log_scale must have H_kv elements")
+        o = torch.empty(B, Hq, T, Dp, device=dev, dtype=cdt)
+        lse = torch.empty(B, Hq, T, device=dev, dtype=torch.float32)
+        stream = _stream_ptr(dev)
+        with torch.cuda.device(dev):
+            check(L.cra_varlen_plan(cu, nd, relay_top_k, table.data_ptr(), stream), "cra_varlen_plan")
+            check(L.cra_relay_build_varlen(kc.data_ptr(), vc.data_ptr(), strides3(kc), strides3(vc), B, Hkv, cu, nd,
+                                           table.data_ptr(), Dp, _dtype_code(cdt), relay_top_k,
+                                           alpha.data_ptr() if alpha is not None else None, gk.data_ptr(),
+                                           gv.data_ptr(), gsrc.data_ptr(), stream), "cra_relay_build_varlen")
+            check(L.cra_fwd_varlen(qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), gk.data_ptr(), gv.data_ptr(),
+                                   strides3(qc), strides3(kc), strides3(vc), B, Hq, Hkv, cu, nd, table.data_ptr(), Dp,
+                                   _dtype_code(cdt), relay_top_k, ctypes.c_float(scale), o.data_ptr(), strides3(o),
+                                   lse.data_ptr(), _err_word(dev).data_ptr(), stream), "cra_fwd_varlen")
+        _raise_on_device_error(dev, "varlen forward")
+        ctx.save_for_backward(qc, kc, vc, o, lse, alpha)
+        ctx.meta = (seqs, kv_groups, relay_top_k, D, Dp, scale, in_dtype, cdt, relay_log_scale is not None)
+        out = o if Dp == D else o[..., :D]
+        return out if out.dtype == in_dtype else out.to(in_dtype)
+
+    @staticmethod
+    def backward(ctx, do):
+        qc, kc, vc, o, lse, alpha = ctx.saved_tensors
+        seqs, kv_groups, top_k, D, Dp, scale, in_dtype, cdt, has_alpha = ctx.meta
+        dev = qc.device
+        L = lib()
+        B, Hq, T, _ = qc.shape
+        Hkv = kc.shape[1]
+        doc_ = _prep(do, cdt, Dp)
+        dq = torch.zeros_like(qc)
+        dk = torch.zeros_like(kc)
+        dv = torch.zeros_like(vc)
+        dalpha = torch.zeros(Hkv, device=dev, dtype=torch.float32) if alpha is not None else None
+        groups = {}
+        for s0, s1 in zip(seqs, seqs[1:]):
+            groups.setdefault(s1 - s0, []).append(s0)
+        stream = _stream_ptr(dev)
+        for n, starts in groups.items():
+            def stack(t):
+                if len(starts) == 1:
+                    return _prep(t.narrow(2, starts[0], n), cdt, Dp)
+                return torch.cat([t.narrow(2, s0, n) for s0 in starts], dim=0)
+            qg, kg, vg, og, dog = (stack(t) for t in (qc, kc, vc, o, doc_))
+            lg = torch.cat([lse.narrow(2, s0, n) for s0 in starts], dim=0).contiguous()
+            G = B * len(starts)
+            use_relay = int(n > RELAY_THRESHOLD)
+            NG = L.cra_global_rows(n, use_relay, top_k)
+            NB = (n + L.cra_window(n) - 1) // L.cra_window(n)
+            gk = torch.empty(G, Hkv, NG, Dp, device=dev, dtype=cdt)
+            gv = torch.empty_like(gk)
+            gsrc = torch.empty(G, Hkv, NB, top_k, device=dev, dtype=torch.int32)
+            a_g = alpha if (alpha is not None and use_relay) else None
+            dqg, dkg, dvg = torch.empty_like(qg), torch.empty_like(kg), torch.empty_like(vg)
+            da = torch.zeros(Hkv, device=dev, dtype=torch.float32) if a_g is not None else None
+            ws_bytes = L.cra_bwd_workspace_bytes(G, Hq, Hkv, n, Dp, use_relay, top_k)
+            ws = torch.empty(max(ws_bytes, 1), device=dev, dtype=torch.uint8)
+            with torch.cuda.device(dev):
+                check(L.cra_relay_build(kg.data_ptr(), vg.data_ptr(), strides3(kg), strides3(vg), G, Hkv, n, Dp,
+                                        _dtype_code(cdt), use_relay, top_k,
+                                        a_g.data_ptr() if a_g is not None else None, gk.data_ptr(), gv.data_ptr(),
+                                        gsrc.data_ptr(), stream), "cra_relay_build")
+                check(L.cra_bwd(qg.data_ptr(), kg.data_ptr(), vg.data_ptr(), og.data_ptr(), dog.data_ptr(),
+                                lg.data_ptr(), gk.data_ptr(), gv.data_ptr(), gsrc.data_ptr(), strides3(qg),
+                                strides3(kg), strides3(vg), strides3(og), strides3(dog), G, Hq, Hkv, n, Dp,
+                                _dtype_code(cdt), use_relay, top_k, ctypes.c_float(scale),
+                                a_g.data_ptr() if a_g is not None else None, dqg.data_ptr(), dkg.data_ptr(),
+                                dvg.data_ptr(), strides3(dqg), strides3(dkg), strides3(dvg),
+                                da.data_ptr() if da is not None else None, ws.data_ptr(), ws_bytes,
+                                _err_word(dev).data_ptr(), stream), "cra_bwd")
+            for i, s0 in enumerate(starts):
+                dq.narrow(2, s0, n).copy_(dqg.narrow(0, i * B, B))
+                dk.narrow(2, s0, n).copy_(dkg.narrow(0, i * B, B))
+                dv.narrow(2, s0, n).copy_(dvg.narrow(0, i * B, B))
+            if da is not None:
+                dalpha += da
+        _raise_on_device_error(dev, "varlen backward")
+
+        def fin(t):
+            t = t if Dp == D else t[..., :D]
+            return t if t.dtype == in_dtype else t.to(in_dtype)
+
+        d_alpha = None
+        if has_alpha:
+            d_alpha = dalpha if dalpha is not None else torch.zeros(Hkv, device=dev, dtype=torch.float32)
+        return fin(dq), fin(dk), fin(dv), None, None, d_alpha, None
+
+
 @torch.compiler.disable
 def cron_root_attention_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                                cu_seqlens: Union[Sequence[int], torch.Tensor], kv_groups: int = 1,
                                use_persistent: bool = False,
                                relay_log_scale: Optional[torch.Tensor] = None,
                                relay_top_k: int = 2) -> torch.Tensor:
-    """Packed variable-length forward (reference core.py:3836-3954): each
-    document [cu_seqlens[i], cu_seqlens[i+1]) is attended independently.
-    ``cu_seqlens`` must be a CPU tensor or a Python sequence.  One call per
-    distinct document length (the reference makes one per document)."""
+    """Packed variable-length attention (reference core.py:3836-3954): each
+    document [cu_seqlens[i], cu_seqlens[i+1]) of the packed sequence
+    dimension attends only to itself, with its own window and relay switch.
+    ``cu_seqlens`` must be a CPU tensor or a Python sequence.  The forward
+    runs as one launch over (document, query tile, head) -- the reference
+    makes one call per document; the backward runs one batched call per
+    distinct document length."""
     if isinstance(cu_seqlens, torch.Tensor):
         if cu_seqlens.device.type != "cpu":
             raise ValueError("cu_seqlens must be a CPU tensor to avoid a device sync on each "
@@ -282,26 +408,8 @@ def cron_root_attention_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor
     if len(seqs) == 2:
         return cron_root_attention_v14(q, k, v, use_persistent=use_persistent, kv_groups=kv_groups,
                                        relay_log_scale=relay_log_scale, relay_top_k=relay_top_k)
-    # Documents of equal length share W and the relay setting, so each such
-    # group runs as ONE batched call (documents stacked along the batch
-    # dimension) instead of one call per document: many short documents fill
-    # the GPU together.  Results are put back in document order.
-    docs = [(s0, s1 - s0) for s0, s1 in zip(seqs, seqs[1:]) if s1 > s0]
-    groups = {}
-    for s0, n in docs:
-        groups.setdefault(n, []).append(s0)
-    B = q.shape[0]
-    out = {}
-    for n, starts in groups.items():
-        if len(starts) == 1:
-            qs, ks, vs = (t.narrow(2, starts[0], n) for t in (q, k, v))
-        else:
-            qs, ks, vs = (torch.cat([t.narrow(2, s0, n) for s0 in starts], dim=0) for t in (q, k, v))
-        o = cron_root_attention_v14(qs, ks, vs, use_persistent=use_persistent, kv_groups=kv_groups,
-                                    relay_log_scale=relay_log_scale, relay_top_k=relay_top_k)
-        for i, s0 in enumerate(starts):
-            out[s0] = o.narrow(0, i * B, B)
-    return torch.cat([out[s0] for s0, _ in docs], dim=2)
+    docs = [seqs[0]] + [b for a, b in zip(seqs, seqs[1:]) if b > a]  # empty documents dropped
+    return _VarlenFunction.apply(q, k, v, docs, kv_groups, relay_log_scale, relay_top_k)
 
 
 def warmup_varlen_shapes(doc_lengths, H: int, D: int, dtype=None, kv_groups: int = 1,

@@ -21,7 +21,8 @@
 namespace cra {
 cudaError_t launch_relay_build(int D, bool bf16, const void* k, const void* v, const int64_t* ks, const int64_t* vs,
                                int B, int Hkv, int S, int W, int top_k, int R, int pos0, const float* log_scale,
-                               void* gk, void* gv, int32_t* gsrc, cudaStream_t stream);
+                               void* gk, void* gv, int32_t* gsrc, cudaStream_t stream, const DocInfo* docs = nullptr,
+                               int n_docs = 0, int NB_total = 0, int NG_total = 0);
 cudaError_t launch_fwd(const QueryPassParams& p, int D, bool bf16, cudaStream_t stream);
 }  // namespace cra
 
@@ -285,6 +286,7 @@ int cra_fwd(const void* q, const void* k, const void* v, const void* g_k, const 
   p.out_ss = o_strides[2];
   p.out_v8 = rows_aligned32(o, o_strides, batch, heads, seq_len);
   p.lse = lse;
+  p.lse_len = seq_len;
   p.delta = nullptr;
   p.B = batch;
   p.H = heads;
@@ -624,6 +626,7 @@ int cra_fwd_shard(const void* q, const void* k, const void* v, const void* g_k, 
   p.out_ss = o_strides[2];
   p.out_v8 = rows_aligned32(o, o_strides, batch, heads, q_len);
   p.lse = lse;
+  p.lse_len = q_len;
   p.B = batch;
   p.H = heads;
   p.kv_groups = heads / kv_heads;
@@ -635,6 +638,142 @@ int cra_fwd_shard(const void* q, const void* k, const void* v, const void* g_k, 
   p.q_begin = static_cast<int>(q_begin);
   p.q_len = q_len;
   p.kv_begin = static_cast<int>(kv_begin);
+  p.scale = softmax_scale;
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.err = dev_error;
+  cudaError_t e = launch_fwd(p, head_dim, bf16, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? CRA_OK : fail(CRA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// packed variable-length batches
+// ---------------------------------------------------------------------------
+namespace {
+
+// Host copy of the document table for cu_seqlens (n_docs + 1 entries);
+// returns the packed global-row count and the totals, or -1 on bad input.
+int64_t varlen_table(const int64_t* cu, int n_docs, int top_k, DocInfo* out, int* n_pairs, int* n_blocks) {
+  if (!cu || n_docs < 1 || cu[0] != 0) return -1;
+  int64_t g = 0, pairs = 0, blks = 0;
+  for (int d = 0; d < n_docs; ++d) {
+    const int64_t len = cu[d + 1] - cu[d];
+    if (len < 1 || cu[d + 1] > INT32_MAX) return -1;
+    const int W = cra_window(len);
+    const int R = rows_per_block(cra_relay_active(len), top_k);
+    const int64_t nb = (len + W - 1) / W;
+    if (out) out[d] = DocInfo{static_cast<int>(cu[d]), static_cast<int>(len), W, R, static_cast<int>(g),
+                              static_cast<int>(pairs), static_cast<int>(blks), 0};
+    g += nb * R;
+    blks += nb;
+    pairs += (len + 2 * kTile - 1) / (2 * kTile);
+    if (g > INT32_MAX || pairs > INT32_MAX) return -1;
+  }
+  if (n_pairs) *n_pairs = static_cast<int>(pairs);
+  if (n_blocks) *n_blocks = static_cast<int>(blks);
+  return g;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t cra_varlen_table_bytes(int n_docs) { return n_docs > 0 ? sizeof(DocInfo) * n_docs : 0; }
+
+int64_t cra_varlen_global_rows(const int64_t* cu_seqlens, int n_docs, int top_k) {
+  if (top_k < 1 || top_k > 4) return -1;
+  return varlen_table(cu_seqlens, n_docs, top_k, nullptr, nullptr, nullptr);
+}
+
+int64_t cra_varlen_blocks(const int64_t* cu_seqlens, int n_docs) {
+  int nb = 0;
+  return varlen_table(cu_seqlens, n_docs, 2, nullptr, nullptr, &nb) < 0 ? -1 : nb;
+}
+
+int cra_varlen_plan(const int64_t* cu_seqlens, int n_docs, int top_k, void* table, void* stream) {
+  if (top_k < 1 || top_k > 4) return fail(CRA_ERR_UNSUPPORTED, "top_k %d outside 1..4", top_k);
+  if (!table) return fail(CRA_ERR_INVALID_ARGUMENT, "table: null pointer");
+  if (varlen_table(cu_seqlens, n_docs, top_k, nullptr, nullptr, nullptr) < 0)
+    return fail(CRA_ERR_INVALID_ARGUMENT, "cu_seqlens must start at 0 and increase strictly (n_docs %d)", n_docs);
+  CRA_TRY(bind_context());
+  // pageable source: cudaMemcpyAsync stages it before returning, so the
+  // temporary may go out of scope
+  DocInfo* host = new DocInfo[n_docs];
+  varlen_table(cu_seqlens, n_docs, top_k, host, nullptr, nullptr);
+  const cudaError_t e = cudaMemcpyAsync(table, host, sizeof(DocInfo) * n_docs, cudaMemcpyHostToDevice,
+                                        static_cast<cudaStream_t>(stream));
+  delete[] host;
+  return e == cudaSuccess ? CRA_OK : fail(CRA_ERR_CUDA, "cudaMemcpyAsync: %s", cudaGetErrorString(e));
+}
+
+int cra_relay_build_varlen(const void* k, const void* v, const int64_t* k_strides, const int64_t* v_strides,
+                           int batch, int kv_heads, const int64_t* cu_seqlens, int n_docs, const void* table,
+                           int head_dim, int dtype, int top_k, const float* relay_log_scale, void* g_k, void* g_v,
+                           int32_t* g_src, void* stream) {
+  int nb = 0;
+  const int64_t NG = varlen_table(cu_seqlens, n_docs, top_k, nullptr, nullptr, &nb);
+  if (NG < 0) return fail(CRA_ERR_INVALID_ARGUMENT, "cu_seqlens must start at 0 and increase strictly");
+  const int64_t T = cu_seqlens[n_docs];
+  CRA_TRY(check_common(batch, kv_heads, kv_heads, static_cast<int>(T), head_dim, dtype, top_k));
+  CRA_TRY(check_tensor("k", k, k_strides, batch, kv_heads));
+  CRA_TRY(check_tensor("v", v, v_strides, batch, kv_heads));
+  if (!g_k || !g_v || !g_src || !table) return fail(CRA_ERR_INVALID_ARGUMENT, "g_k / g_v / g_src / table: null");
+  if (!aligned16(g_k) || !aligned16(g_v)) return fail(CRA_ERR_MISALIGNED, "g_k / g_v: not 16-byte aligned");
+  cudaError_t e = launch_relay_build(head_dim, dtype == CRA_BF16, k, v, k_strides, v_strides, batch, kv_heads,
+                                     static_cast<int>(T), 1, top_k, 1, 0, relay_log_scale, g_k, g_v, g_src,
+                                     static_cast<cudaStream_t>(stream), static_cast<const DocInfo*>(table), n_docs, nb,
+                                     static_cast<int>(NG));
+  return e == cudaSuccess ? CRA_OK : fail(CRA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+}
+
+int cra_fwd_varlen(const void* q, const void* k, const void* v, const void* g_k, const void* g_v,
+                   const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, int batch, int heads,
+                   int kv_heads, const int64_t* cu_seqlens, int n_docs, const void* table, int head_dim, int dtype,
+                   int top_k, float softmax_scale, void* o, const int64_t* o_strides, float* lse, int* dev_error,
+                   void* stream) {
+  int n_pairs = 0;
+  const int64_t NG = varlen_table(cu_seqlens, n_docs, top_k, nullptr, &n_pairs, nullptr);
+  if (NG < 0) return fail(CRA_ERR_INVALID_ARGUMENT, "cu_seqlens must start at 0 and increase strictly");
+  const int64_t T = cu_seqlens[n_docs];
+  CRA_TRY(check_common(batch, heads, kv_heads, static_cast<int>(T), head_dim, dtype, top_k));
+  CRA_TRY(check_tensor("q", q, q_strides, batch, heads));
+  CRA_TRY(check_tensor("k", k, k_strides, batch, kv_heads));
+  CRA_TRY(check_tensor("v", v, v_strides, batch, kv_heads));
+  CRA_TRY(check_tensor("o", o, o_strides, batch, heads));
+  if (!g_k || !g_v || !lse || !table) return fail(CRA_ERR_INVALID_ARGUMENT, "g_k / g_v / lse / table: null");
+  if (!aligned16(g_k) || !aligned16(g_v)) return fail(CRA_ERR_MISALIGNED, "g_k / g_v: not 16-byte aligned");
+  if (!(softmax_scale > 0.f) || !std::isfinite(softmax_scale))
+    return fail(CRA_ERR_INVALID_ARGUMENT, "softmax_scale must be finite and > 0");
+  const bool bf16 = dtype == CRA_BF16;
+  const int64_t g_st[3] = {static_cast<int64_t>(kv_heads) * NG * head_dim, NG * head_dim, head_dim};
+  CRA_TRY(bind_context());
+  QueryPassParams p;
+  std::memset(&p, 0, sizeof(p));
+  CRA_TRY(make_tmap("q", &p.tm_q, q, bf16, head_dim, T, heads, batch, q_strides));
+  CRA_TRY(make_tmap("k", &p.tm_k, k, bf16, head_dim, T, kv_heads, batch, k_strides));
+  CRA_TRY(make_tmap("v", &p.tm_v, v, bf16, head_dim, T, kv_heads, batch, v_strides));
+  CRA_TRY(make_tmap("g_k", &p.tm_gk, g_k, bf16, head_dim, NG, kv_heads, batch, g_st));
+  CRA_TRY(make_tmap("g_v", &p.tm_gv, g_v, bf16, head_dim, NG, kv_heads, batch, g_st));
+  p.tm_do = p.tm_q;
+  p.out = o;
+  p.out_sb = o_strides[0];
+  p.out_sh = o_strides[1];
+  p.out_ss = o_strides[2];
+  p.out_v8 = rows_aligned32(o, o_strides, batch, heads, T);
+  p.lse = lse;
+  p.lse_len = static_cast<int>(T);
+  p.B = batch;
+  p.H = heads;
+  p.kv_groups = heads / kv_heads;
+  p.S = static_cast<int>(T);
+  p.W = 1;
+  p.R = 1;
+  p.NG = static_cast<int>(NG);
+  p.q_len = static_cast<int>(T);
+  p.docs = static_cast<const DocInfo*>(table);
+  p.n_docs = n_docs;
+  p.n_pairs_total = n_pairs;
   p.scale = softmax_scale;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   p.err = dev_error;

@@ -88,12 +88,34 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_pairs = (p.q_len + 2 * kTile - 1) / (2 * kTile);
-  const int pr = n_pairs - 1 - static_cast<int>(blockIdx.x);  // longest pairs first
   const int h = blockIdx.y, b = blockIdx.z, hk = h / p.kv_groups;
-  const int m0 = p.q_begin + pr * 2 * kTile;  // absolute position of the first query
-  const int W = p.W, R = p.R;
-  const int q_end = p.q_begin + p.q_len;
+  // Positions below are in the coordinates of one sequence; these offsets
+  // map them to tensor rows: Q / O rows (qoff), K / V rows (koff), global
+  // rows (goff).  A packed variable-length batch maps each CTA to one
+  // document (docs table); a sequence shard offsets by its begin.
+  int q_begin = p.q_begin, q_len = p.q_len, W = p.W, R = p.R, pr;
+  int qoff = -p.q_begin, koff = -p.kv_begin, goff = 0;
+  if (p.docs) {
+    int lo = 0, hi = p.n_docs - 1;  // last document whose pair0 <= blockIdx.x
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (p.docs[mid].pair0 <= static_cast<int>(blockIdx.x)) lo = mid; else hi = mid - 1;
+    }
+    const DocInfo dc = p.docs[lo];
+    q_begin = 0;
+    q_len = dc.len;
+    W = dc.W;
+    R = dc.R;
+    qoff = koff = dc.start;
+    goff = dc.g0;
+    const int np = (dc.len + 2 * kTile - 1) / (2 * kTile);
+    pr = np - 1 - (static_cast<int>(blockIdx.x) - dc.pair0);  // longest pairs of the document first
+  } else {
+    const int n_pairs = (p.q_len + 2 * kTile - 1) / (2 * kTile);
+    pr = n_pairs - 1 - static_cast<int>(blockIdx.x);  // longest pairs first
+  }
+  const int m0 = q_begin + pr * 2 * kTile;  // position of the first query
+  const int q_end = q_begin + q_len;
   const PairSchedule sch(m0, q_end, W, R);
 
   const uint32_t sbase = smem_u32(smem);
@@ -139,7 +161,7 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
       for (int x = 0; x < nq; ++x)
         for (int c = 0; c < D / 64; ++c)
           tma_load_4d(sbase + C::OFF_Q + x * C::TB + c * kTile * 128, &p.tm_q, BAR(C::B_QFULL), c * 64,
-                      m0 + x * kTile - p.q_begin, h, b);
+                      m0 + x * kTile + qoff, h, b);
       // band keys of this pair from the edge copy when its window reaches
       // below this shard's own K / V rows
       const bool use_edge = p.has_edge && local_start(m0, W) < p.kv_begin;
@@ -160,7 +182,7 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
         mbar_expect_tx(BAR(C::B_FULL + sl), C::TB);
         for (int c = 0; c < D / 64; ++c)
           tma_load_4d(sbase + C::OFF_RING + sl * C::TB + c * kTile * 128, m, BAR(C::B_FULL + sl), c * 64,
-                      g ? row0 : row0 - (use_edge ? p.edge_begin : p.kv_begin), hk, b);
+                      g ? row0 + goff : use_edge ? row0 - p.edge_begin : row0 + koff, hk, b);
         ++issued;
       }
       // Do not leave while copies into this CTA's shared memory are in
@@ -369,7 +391,7 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
       tc_fence_after();
       const float inv = 1.f / fmaxf(l_run, 1e-6f);
       typename E::T* orow = reinterpret_cast<typename E::T*>(p.out) + b * p.out_sb + h * p.out_sh +
-                            static_cast<int64_t>(qi - p.q_begin) * p.out_ss;
+                            static_cast<int64_t>(qi + qoff) * p.out_ss;
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         float o[32];
@@ -386,7 +408,7 @@ __global__ void __launch_bounds__(320, 1) fwd_kernel(const __grid_constant__ Que
         }
       }
       if (row_ok)
-        p.lse[(static_cast<int64_t>(b) * p.H + h) * p.q_len + (qi - p.q_begin)] =
+        p.lse[(static_cast<int64_t>(b) * p.H + h) * p.lse_len + (qi + qoff)] =
             (m_run + log2f(fmaxf(l_run, 1e-6f))) * 0.69314718055994531f;
     }
   }
@@ -415,7 +437,7 @@ static cudaError_t launch_fwd_t(const QueryPassParams& p, cudaStream_t stream) {
   auto kern = fwd_kernel<D, BF16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
-  dim3 grid((p.q_len + 2 * kTile - 1) / (2 * kTile), p.H, p.B);
+  dim3 grid(p.docs ? p.n_pairs_total : (p.q_len + 2 * kTile - 1) / (2 * kTile), p.H, p.B);
   kern<<<grid, 320, C::SMEM, stream>>>(p);
   return cudaGetLastError();
 }

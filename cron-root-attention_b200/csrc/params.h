@@ -7,6 +7,15 @@
 
 namespace cra {
 
+// One document of a packed variable-length batch (device table, built by
+// cra_varlen_plan): rows [start, start + len) of the packed sequence, its
+// own window W and global rows per block R, the first row of its global
+// rows in the packed list, and prefix counts of query-tile pairs and
+// W-blocks over the earlier documents.
+struct DocInfo {
+  int start, len, W, R, g0, pair0, blk0, pad;
+};
+
 // Query-centric attention pass (forward, and the dQ pass of the backward).
 struct alignas(64) QueryPassParams {
   CUtensorMap tm_q;   // [B, H,   S,  D]
@@ -22,6 +31,11 @@ struct alignas(64) QueryPassParams {
   CUtensorMap tm_ke;
   CUtensorMap tm_ve;
   int has_edge, edge_begin;
+  // Packed variable-length batch (forward): one CTA per query-tile pair of
+  // every document; null for a single sequence.
+  const DocInfo* docs;
+  int n_docs, n_pairs_total;
+  int lse_len;        // row stride of lse per (b, h): q_len, or the packed length
   void* out;          // forward: O;  backward: dQ  (element strides below)
   int64_t out_sb, out_sh, out_ss;
   int out_v8;         // every output row starts on a 32-byte boundary: 32-byte stores allowed

@@ -42,17 +42,37 @@ __global__ void __launch_bounds__(128) relay_build_kernel(const void* __restrict
                                                           int64_t v_sh, int64_t v_ss, int Hkv, int S, int W, int NB,
                                                           int top_k, int R, int pos0, const float* __restrict__ log_scale,
                                                           void* __restrict__ gkp, void* __restrict__ gvp,
-                                                          int32_t* __restrict__ gsrc) {
+                                                          int32_t* __restrict__ gsrc, const DocInfo* __restrict__ docs,
+                                                          int n_docs, int NG) {
   using E = Elt<BF16>;
   using T = typename E::T;
   constexpr int LPR = D / 8;          // lanes per row
   constexpr int RPS = 32 / LPR;       // rows per warp step
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r = blockIdx.x * 4 + warp;
+  int r = blockIdx.x * 4 + warp;
   const int h = blockIdx.y, b = blockIdx.z;
   if (r >= NB) return;
   const T* k = reinterpret_cast<const T*>(kp) + b * k_sb + h * k_sh;
   const T* v = reinterpret_cast<const T*>(vp) + b * v_sb + h * v_sh;
+  // output: global rows from g_row, source slot from src_slot
+  int64_t g_row = (static_cast<int64_t>(b) * Hkv + h) * static_cast<int64_t>(NB) * R + static_cast<int64_t>(r) * R;
+  int64_t src_slot = (static_cast<int64_t>(b) * Hkv + h) * NB + r;
+  if (docs) {  // packed variable-length batch: block r of the whole batch -> document, local block
+    int lo = 0, hi = n_docs - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (docs[mid].blk0 <= r) lo = mid; else hi = mid - 1;
+    }
+    const DocInfo dc = docs[lo];
+    k += static_cast<int64_t>(dc.start) * k_ss;
+    v += static_cast<int64_t>(dc.start) * v_ss;
+    S = dc.len;
+    W = dc.W;
+    R = dc.R;
+    r -= dc.blk0;
+    g_row = (static_cast<int64_t>(b) * Hkv + h) * NG + dc.g0 + static_cast<int64_t>(r) * R;
+    // src_slot stays the batch-wide block index; positions are document-local
+  }
   const int row_lo = r * W;
   const int row_hi = min(row_lo + W, S);
   const int sub = lane / LPR, part = lane % LPR;
@@ -121,8 +141,8 @@ __global__ void __launch_bounds__(128) relay_build_kernel(const void* __restrict
   }
 
   // Write the block's R global rows: strided row, then top_k relay rows.
-  T* gk = reinterpret_cast<T*>(gkp) + ((static_cast<int64_t>(b) * Hkv + h) * NB + r) * R * D;
-  T* gv = reinterpret_cast<T*>(gvp) + ((static_cast<int64_t>(b) * Hkv + h) * NB + r) * R * D;
+  T* gk = reinterpret_cast<T*>(gkp) + g_row * D;
+  T* gv = reinterpret_cast<T*>(gvp) + g_row * D;
   float sc = 1.f;
   if (log_scale) sc = E::to_f(E::from_f(expf(log_scale[h])));
   // each row: D/8 16-byte units; the warp covers RPS rows per pass
@@ -154,7 +174,7 @@ __global__ void __launch_bounds__(128) relay_build_kernel(const void* __restrict
       *reinterpret_cast<uint4*>(gk + t * D + part * 8) = uk;
       *reinterpret_cast<uint4*>(gv + t * D + part * 8) = uv;
       if (t > 0 && part == 0 && gsrc)
-        gsrc[((static_cast<int64_t>(b) * Hkv + h) * NB + r) * top_k + (t - 1)] = src + pos0;
+        gsrc[src_slot * top_k + (t - 1)] = src + pos0;
     }
   }
 }
@@ -162,12 +182,13 @@ __global__ void __launch_bounds__(128) relay_build_kernel(const void* __restrict
 // host-side launcher (called from capi.cu)
 cudaError_t launch_relay_build(int D, bool bf16, const void* k, const void* v, const int64_t* ks, const int64_t* vs,
                                int B, int Hkv, int S, int W, int top_k, int R, int pos0, const float* log_scale,
-                               void* gk, void* gv, int32_t* gsrc, cudaStream_t stream) {
-  const int NB = (S + W - 1) / W;
+                               void* gk, void* gv, int32_t* gsrc, cudaStream_t stream, const DocInfo* docs,
+                               int n_docs, int NB_total, int NG_total) {
+  const int NB = docs ? NB_total : (S + W - 1) / W;
   dim3 grid((NB + 3) / 4, Hkv, B);
 #define CRA_RELAY(DD, BB)                                                                                          \
   relay_build_kernel<DD, BB><<<grid, 128, 0, stream>>>(k, v, ks[0], ks[1], ks[2], vs[0], vs[1], vs[2], Hkv, S, W, \
-                                                       NB, top_k, R, pos0, log_scale, gk, gv, gsrc)
+                                                       NB, top_k, R, pos0, log_scale, gk, gv, gsrc, docs, n_docs, NG_total)
   if (D == 128) {
     if (bf16) CRA_RELAY(128, true); else CRA_RELAY(128, false);
   } else {

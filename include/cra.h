@@ -131,6 +131,37 @@ int cra_fwd_shard(const void* q, const void* k, const void* v, const void* g_k, 
                   int64_t edge_begin, int edge_len, int head_dim, int dtype, int use_relay, int top_k,
                   float softmax_scale, void* o, const int64_t* o_strides, float* lse, int* dev_error, void* stream);
 
+/* Packed variable-length batches (documents of different lengths
+ * concatenated along the sequence dimension; every document attends only to
+ * itself, with its own W = ceil(sqrt(len)) and relay switch).  cu_seqlens is
+ * a HOST array of n_docs + 1 increasing offsets starting at 0; the packed
+ * length is cu_seqlens[n_docs].
+ *   cra_varlen_plan writes the device document table (caller-allocated,
+ *   cra_varlen_table_bytes(n_docs) bytes) on `stream`;
+ *   cra_relay_build_varlen builds every document's global rows into one
+ *   packed list g_k / g_v [batch, kv_heads, cra_varlen_global_rows(), D]
+ *   (document d's rows after document d - 1's) and g_src [batch, kv_heads,
+ *   cra_varlen_blocks(), top_k] (positions local to the document) -- one
+ *   launch for all documents;
+ *   cra_fwd_varlen computes every document's forward -- one launch over
+ *   (document, query-tile pair, head); lse is [batch, heads, packed length].
+ * Replaces the per-document loop of cron_root_attention_varlen, core.py:
+ * 3837-3954 (each document there is a separate cron_root_attention_v14
+ * call). */
+size_t cra_varlen_table_bytes(int n_docs);
+int64_t cra_varlen_global_rows(const int64_t* cu_seqlens, int n_docs, int top_k);
+int64_t cra_varlen_blocks(const int64_t* cu_seqlens, int n_docs);
+int cra_varlen_plan(const int64_t* cu_seqlens, int n_docs, int top_k, void* table, void* stream);
+int cra_relay_build_varlen(const void* k, const void* v, const int64_t* k_strides, const int64_t* v_strides,
+                           int batch, int kv_heads, const int64_t* cu_seqlens, int n_docs, const void* table,
+                           int head_dim, int dtype, int top_k, const float* relay_log_scale, void* g_k, void* g_v,
+                           int32_t* g_src, void* stream);
+int cra_fwd_varlen(const void* q, const void* k, const void* v, const void* g_k, const void* g_v,
+                   const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, int batch, int heads,
+                   int kv_heads, const int64_t* cu_seqlens, int n_docs, const void* table, int head_dim, int dtype,
+                   int top_k, float softmax_scale, void* o, const int64_t* o_strides, float* lse, int* dev_error,
+                   void* stream);
+
 /* Bytes of device workspace cra_bwd needs for these sizes (256-byte aligned
  * base required). */
 size_t cra_bwd_workspace_bytes(int batch, int heads, int kv_heads, int seq_len, int head_dim, int use_relay,

@@ -52,33 +52,15 @@ def test_gpu_info_without_gpu():
         assert cra.get_num_sms() == 1
 
 
-def test_varlen_groups_equal_lengths_into_one_call(monkeypatch):
-    """Equal-length documents run as one batched call; the result equals the
-    per-document computation (op replaced by the CPU oracle here)."""
+def test_varlen_argument_checks():
+    """cu_seqlens must start at 0, end at the packed length and not decrease,
+    and live on the host; CPU tensors are refused (no CPU fallback)."""
+    import pytest
     import torch
     import cron_root_attention as cra
-    from cron_root_attention import core
-    from oracle import cra_oracle as O
-
-    calls = []
-
-    def oracle_op(q, k, v, use_persistent=False, kv_groups=1, relay_log_scale=None, relay_top_k=2):
-        calls.append(tuple(q.shape))
-        return O.forward(q, k, v, kv_groups=kv_groups, top_k=relay_top_k, dtype=torch.float64)[0]
-
-    monkeypatch.setattr(core, "cron_root_attention_v14", oracle_op)
-    g = torch.Generator().manual_seed(5)
-    lens = [300, 120, 300, 0, 57, 120, 300]
-    S = sum(lens)
-    cu = [0]
-    for n in lens:
-        cu.append(cu[-1] + n)
-    q = torch.randn(2, 4, S, 16, generator=g, dtype=torch.float64)
-    k = torch.randn(2, 2, S, 16, generator=g, dtype=torch.float64)
-    v = torch.randn(2, 2, S, 16, generator=g, dtype=torch.float64)
-    o = cra.cron_root_attention_varlen(q, k, v, cu, kv_groups=2)
-    assert sorted(calls) == sorted([(6, 4, 300, 16), (4, 4, 120, 16), (2, 4, 57, 16)])
-    for s0, s1 in zip(cu, cu[1:]):
-        if s1 > s0:
-            ref = O.forward(q[:, :, s0:s1], k[:, :, s0:s1], v[:, :, s0:s1], kv_groups=2, dtype=torch.float64)[0]
-            assert (o[:, :, s0:s1] - ref).abs().max().item() < 1e-12
+    q = torch.zeros(1, 2, 10, 16)
+    for bad in ([1, 10], [0, 9], [0, 6, 4, 10]):
+        with pytest.raises(ValueError):
+            cra.cron_root_attention_varlen(q, q, q, bad)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        cra.cron_root_attention_varlen(q, q, q, [0, 4, 10])

@@ -99,3 +99,20 @@ def test_wait_probe_library_loads():
     from test_wait_timeout_gpu import PROBE
     h = ctypes.CDLL(PROBE)
     assert hasattr(h, "cra_test_wait_timeout")
+
+
+def test_varlen_plan_sizes(L):
+    """Packed global rows and blocks of a varlen batch: each document with its
+    own W = ceil(sqrt(len)) and relay switch (len > 2048)."""
+    cu = (ctypes.c_int64 * 4)(0, 1000, 3100, 5000)
+    exp_rows, exp_blocks = 0, 0
+    for n in (1000, 2100, 1900):
+        W = O.window(n)
+        nb = (n + W - 1) // W
+        exp_rows += nb * (3 if n > 2048 else 1)
+        exp_blocks += nb
+    assert L.cra_varlen_global_rows(cu, 3, 2) == exp_rows
+    assert L.cra_varlen_blocks(cu, 3) == exp_blocks
+    assert L.cra_varlen_table_bytes(3) == 3 * 32
+    bad = (ctypes.c_int64 * 3)(0, 10, 10)
+    assert L.cra_varlen_global_rows(bad, 2, 2) == -1

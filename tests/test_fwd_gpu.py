@@ -268,3 +268,32 @@ def test_output_rows_only_16_byte_aligned(cuda_device):
     torch.cuda.synchronize(dev)
     assert torch.equal(outs[0][1], outs[1][1])
     assert torch.count_nonzero(outs[1][0][..., D:]) == 0  # nothing written past the row
+
+
+def test_varlen_mixed_lengths_one_launch_forward_backward(cuda_device):
+    """Documents of different lengths (with and without the relay, one
+    shorter than a tile, grouped K/V heads, a relay scale) through the
+    single-launch varlen forward and the grouped backward, against the oracle
+    per document."""
+    cra = _cra()
+    dev = cuda_device
+    cu = [0, 100, 2600, 2700, 5300, 5429]  # lengths 100, 2500, 100, 2600, 129
+    Hq, Hkv = 4, 2
+    q, k, v, do = inputs(1, Hq, Hkv, cu[-1], 64, torch.bfloat16, 39, with_do=True)
+    a = torch.tensor([0.2, -0.3])
+    qd, kd, vd = (t.to(dev).requires_grad_(True) for t in (q, k, v))
+    ad = a.to(dev).requires_grad_(True)
+    o = cra.cron_root_attention_varlen(qd, kd, vd, cu, kv_groups=2, relay_log_scale=ad)
+    o.backward(do.to(dev))
+    torch.cuda.synchronize(dev)
+    assert cra.check_device_errors(dev) == 0
+    from parity import GRAD_REL_L2, rel_l2
+    for s0, s1 in zip(cu, cu[1:]):
+        sl = lambda t: t[:, :, s0:s1]
+        ro, rdq, rdk, rdv, _ = O.forward_backward(sl(q), sl(k), sl(v), sl(do), kv_groups=2, relay_log_scale=a,
+                                                  relay_dtype=torch.bfloat16)
+        r = fwd_check(sl(o), ro, torch.bfloat16)
+        assert r["ok"], (s0, r)
+        for name, x, y in (("dq", sl(qd.grad), rdq), ("dk", sl(kd.grad), rdk), ("dv", sl(vd.grad), rdv)):
+            assert rel_l2(x, y) <= GRAD_REL_L2, (s0, name, rel_l2(x, y))
+    assert ad.grad is not None and torch.isfinite(ad.grad).all()
