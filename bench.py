@@ -217,13 +217,13 @@ def run_reference(args, rank, world):
 # bf16, scaled by H / 8 (every kernel's traffic grows in proportion to the
 # heads).  None where no capture of the current kernel exists.
 TRAFFIC_H8 = {
-    "fwd_kernel": None,
-    "relay_build_kernel": None,
-    "delta_kernel": None,
-    "keyglobal_kernel": None,
-    "reduce_kernel": None,
-    "keylocal_kernel": None,
-    "dq_kernel": None,
+    "fwd_kernel": 528.839680e6,
+    "relay_build_kernel": 141.839616e6,
+    "delta_kernel": 277.032192e6,
+    "keyglobal_kernel": 375.778048e6,
+    "reduce_kernel": 123.899136e6,
+    "keylocal_kernel": 788.465664e6,
+    "dq_kernel": 663.429632e6,
     "dq_convert_kernel": None,
 }
 
