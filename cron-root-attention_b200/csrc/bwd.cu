@@ -348,6 +348,30 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
             tma_load_4d(sbase + C::OFF_DO + c * kTile * 128, &p.tm_do, BAR(C::B_QFULL), c * 64, tl.m0, tl.h, tl.b);
           }
           ++nq;
+#ifndef CRA_DQ_NO_PREFETCH
+          // the next tile's Q / dO and first K / V units into L2: its Q / dO
+          // load can only start once this tile's last scores are issued
+          if (t + static_cast<int>(gridDim.x) < n_tiles) {
+            const DqTile tn(t + gridDim.x, p.n_qtiles, p.H);
+            const DqUnits un2(tn.m0, S, W, R);
+            for (int c = 0; c < D / 64; ++c) {
+              tma_prefetch_l2_4d(&p.tm_q, c * 64, tn.m0, tn.h, tn.b);
+              tma_prefetch_l2_4d(&p.tm_do, c * 64, tn.m0, tn.h, tn.b);
+            }
+            int np = 0;
+            for (int j = 0; j < un2.ntiles && np < 4; ++j)
+              for (int hh = 0; hh < 2 && np < 4; ++hh) {
+                int row0;
+                bool g;
+                if (!un2.get(j, hh, row0, g)) continue;
+                ++np;
+                for (int c = 0; c < D / 64; ++c) {
+                  tma_prefetch_l2_4d(g ? &p.tm_gk : &p.tm_k, c * 64, row0, tn.h / p.kv_groups, tn.b);
+                  tma_prefetch_l2_4d(g ? &p.tm_gv : &p.tm_v, c * 64, row0, tn.h / p.kv_groups, tn.b);
+                }
+              }
+          }
+#endif
           return true;
         };
         int lu = 0;  // units of this tile issued
