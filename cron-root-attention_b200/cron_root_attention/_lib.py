@@ -47,6 +47,13 @@ _SIGNATURES = {
                                     _vp]),
     "cra_fwd_varlen": (_i, [_vp, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _i, _i, _i, _i64p, _i, _vp, _i, _i, _i, _f,
                             _vp, _i64p, _vp, _vp, _vp]),
+    "cra_bwd_shard_workspace_bytes": (ctypes.c_size_t, [_i, _i, _i, ctypes.c_int64, _i, _i, _i, _i]),
+    "cra_bwd_shard_global": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _i, _i, _i, ctypes.c_int64,
+                                  ctypes.c_int64, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp, ctypes.c_size_t, _vp, _vp]),
+    "cra_bwd_shard_local": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _i64p, _vp, _vp, _i64p, _i64p,
+                                 ctypes.c_int64, _i, _i, _i, _i, ctypes.c_int64, ctypes.c_int64, _i, _i, _i, _i, _i,
+                                 _f, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _i64p, _i64p, _vp,
+                                 _vp, ctypes.c_size_t, _vp, _vp]),
     "cra_bwd_workspace_bytes": (ctypes.c_size_t, [_i, _i, _i, _i, _i, _i, _i]),
     "cra_bwd_fused_workspace_bytes": (ctypes.c_size_t, [_i, _i, _i, _i, _i, _i, _i]),
     "cra_bwd": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64p, _i64p, _i64p, _i64p, _i64p,

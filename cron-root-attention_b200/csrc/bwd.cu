@@ -255,11 +255,11 @@ struct DqUnits {
 // Query tile t of the persistent dQ walk: consecutive t are consecutive tiles
 // of one (b, h) (their band keys overlap in L2), latest queries first.
 struct DqTile {
-  int m0, h, b;
-  __device__ __forceinline__ DqTile(int t, int n_qtiles, int H) {
+  int m0, h, b;  // m0: absolute position of the tile's first query (tiles start at q_lo)
+  __device__ __forceinline__ DqTile(int t, int n_qtiles, int H, int q_lo) {
     const int qt = n_qtiles - 1 - t % n_qtiles;
     const int bh = t / n_qtiles;
-    m0 = qt * kTile;
+    m0 = q_lo + qt * kTile;
     h = bh % H;
     b = bh / H;
   }
@@ -297,6 +297,8 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int W = p.W, S = p.S, R = p.R;
   const int Spad = p.n_qtiles * kTile;
+  const int q_end = p.q_begin + p.q_len;  // queries [q_begin, q_end) (the whole sequence, or a shard)
+  (void)S;
   const int n_tiles = p.n_qtiles * p.H * p.B;
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + C::OFF_BAR;
@@ -335,39 +337,41 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
       int e = 0, nq = 0;  // ring entries issued, Q / dO tiles issued
       bool ok = true;
       for (int t = blockIdx.x, it = 0; ok && t < n_tiles; t += gridDim.x, ++it) {
-        const DqTile tl(t, p.n_qtiles, p.H);
+        const DqTile tl(t, p.n_qtiles, p.H, p.q_begin);
         const int hk = tl.h / p.kv_groups;
-        const DqUnits un(tl.m0, S, W, R);
+        const DqUnits un(tl.m0, q_end, W, R);
         auto load_q = [&]() -> bool {
           PROF_T(t0);
           if (it > 0 && !mbar_wait(BAR(C::B_QEMPTY), (it - 1) & 1, ab)) return false;
           PROF_ADD(0, t0);
           mbar_expect_tx(BAR(C::B_QFULL), 2 * C::TB);
           for (int c = 0; c < D / 64; ++c) {
-            tma_load_4d(sbase + C::OFF_Q + c * kTile * 128, &p.tm_q, BAR(C::B_QFULL), c * 64, tl.m0, tl.h, tl.b);
-            tma_load_4d(sbase + C::OFF_DO + c * kTile * 128, &p.tm_do, BAR(C::B_QFULL), c * 64, tl.m0, tl.h, tl.b);
+            tma_load_4d(sbase + C::OFF_Q + c * kTile * 128, &p.tm_q, BAR(C::B_QFULL), c * 64, tl.m0 - p.q_begin, tl.h, tl.b);
+            tma_load_4d(sbase + C::OFF_DO + c * kTile * 128, &p.tm_do, BAR(C::B_QFULL), c * 64, tl.m0 - p.q_begin, tl.h, tl.b);
           }
           ++nq;
 #ifndef CRA_DQ_NO_PREFETCH
           // the next tile's Q / dO and first K / V units into L2: its Q / dO
           // load can only start once this tile's last scores are issued
           if (t + static_cast<int>(gridDim.x) < n_tiles) {
-            const DqTile tn(t + gridDim.x, p.n_qtiles, p.H);
-            const DqUnits un2(tn.m0, S, W, R);
+            const DqTile tn(t + gridDim.x, p.n_qtiles, p.H, p.q_begin);
+            const DqUnits un2(tn.m0, q_end, W, R);
             for (int c = 0; c < D / 64; ++c) {
-              tma_prefetch_l2_4d(&p.tm_q, c * 64, tn.m0, tn.h, tn.b);
-              tma_prefetch_l2_4d(&p.tm_do, c * 64, tn.m0, tn.h, tn.b);
+              tma_prefetch_l2_4d(&p.tm_q, c * 64, tn.m0 - p.q_begin, tn.h, tn.b);
+              tma_prefetch_l2_4d(&p.tm_do, c * 64, tn.m0 - p.q_begin, tn.h, tn.b);
             }
             int np = 0;
             for (int j = 0; j < un2.ntiles && np < 4; ++j)
               for (int hh = 0; hh < 2 && np < 4; ++hh) {
                 int row0;
                 bool g;
-                if (!un2.get(j, hh, row0, g)) continue;
+                if (!un2.get(j, hh, row0, g) || (!g && p.has_edge && row0 < p.kv_begin)) continue;
                 ++np;
                 for (int c = 0; c < D / 64; ++c) {
-                  tma_prefetch_l2_4d(g ? &p.tm_gk : &p.tm_k, c * 64, row0, tn.h / p.kv_groups, tn.b);
-                  tma_prefetch_l2_4d(g ? &p.tm_gv : &p.tm_v, c * 64, row0, tn.h / p.kv_groups, tn.b);
+                  tma_prefetch_l2_4d(g ? &p.tm_gk : &p.tm_k, c * 64, g ? row0 : row0 - p.kv_begin, tn.h / p.kv_groups,
+                                     tn.b);
+                  tma_prefetch_l2_4d(g ? &p.tm_gv : &p.tm_v, c * 64, g ? row0 : row0 - p.kv_begin, tn.h / p.kv_groups,
+                                     tn.b);
                 }
               }
           }
@@ -389,11 +393,14 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
                 break;
               }
               PROF_ADD(1, t0);
-              const CUtensorMap* m = g ? (kv ? &p.tm_gv : &p.tm_gk) : (kv ? &p.tm_v : &p.tm_k);
+              // band units below this shard's own K / V rows: the halo (edge copy)
+              const bool edge = !g && p.has_edge && row0 < p.kv_begin;
+              const CUtensorMap* m = g ? (kv ? &p.tm_gv : &p.tm_gk)
+                                       : edge ? (kv ? &p.tm_ve : &p.tm_ke) : (kv ? &p.tm_v : &p.tm_k);
               mbar_expect_tx(BAR(C::B_FULL + sl), C::UB);
               for (int c = 0; c < D / 64; ++c)
                 tma_load_4d(sbase + C::OFF_RING + sl * C::UB + c * kUnit * 128, m, BAR(C::B_FULL + sl), c * 64,
-                            row0, hk, tl.b);
+                            g ? row0 : edge ? row0 - p.edge_begin : row0 - p.kv_begin, hk, tl.b);
             }
           }
         if (ok && lu <= C::QPRE && !load_q()) ok = false;
@@ -439,8 +446,8 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
       int pit = -1;                                  // tile iteration of unit u - 1
       bool pfirst = false;                           // unit u - 1 was its tile's first
       for (int t = blockIdx.x, it = 0; ok && t < n_tiles; t += gridDim.x, ++it) {
-        const DqTile tl(t, p.n_qtiles, p.H);
-        const DqUnits un(tl.m0, S, W, R);
+        const DqTile tl(t, p.n_qtiles, p.H, p.q_begin);
+        const DqUnits un(tl.m0, q_end, W, R);
         PROF_T(tq);
         if (!warp_wait(BAR(C::B_QFULL), it & 1, ab)) { ok = false; break; }
         PROF_ADD(6, tq);
@@ -505,13 +512,13 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
     bool ok = true;
     int u = 0;
     for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x) {
-      const DqTile tl(t, p.n_qtiles, p.H);
-      const DqUnits un(tl.m0, S, W, R);
+      const DqTile tl(t, p.n_qtiles, p.H, p.q_begin);
+      const DqUnits un(tl.m0, q_end, W, R);
       const int qi = tl.m0 + r;
-      const bool row_ok = qi < S;
+      const bool row_ok = qi < q_end;
       const int ls = local_start(qi, W);
       const int cnt = gcount(qi, W, R);
-      const int64_t rowi = (static_cast<int64_t>(tl.b) * p.H + tl.h) * Spad + qi;
+      const int64_t rowi = (static_cast<int64_t>(tl.b) * p.H + tl.h) * Spad + (qi - p.q_begin);
       const float nl = p.lse[rowi];    // -lse * log2(e), padded array
       const float nd = p.delta[rowi];  // -Di
       const float2 sl2x2 = make_float2(sl2, sl2), nlx2 = make_float2(nl, nl), ndx2 = make_float2(nd, nd);
@@ -578,7 +585,7 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
     const int r = ((warp & 3) << 5) | lane;
     const uint32_t lane_off = static_cast<uint32_t>(r & ~31) << 16;
     for (int t = blockIdx.x, it = 0; t < n_tiles; t += gridDim.x, ++it) {
-      const DqTile tl(t, p.n_qtiles, p.H);
+      const DqTile tl(t, p.n_qtiles, p.H, p.q_begin);
       const int acc = it & 1;
       PROF_T(t0);
       if (!mbar_wait(BAR(C::B_ACCFULL + acc), (it >> 1) & 1, ab)) break;
@@ -596,9 +603,9 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
       tc_fence_before();
       mbar_arrive(BAR(C::B_ACCFREE + acc));
       const int qi = tl.m0 + r;
-      if (qi < S) {
+      if (qi < q_end) {
         typename E::T* orow = reinterpret_cast<typename E::T*>(p.out) + tl.b * p.out_sb + tl.h * p.out_sh +
-                              static_cast<int64_t>(qi) * p.out_ss;
+                              static_cast<int64_t>(qi - p.q_begin) * p.out_ss;
 #pragma unroll
         for (int q = 0; q < D / 16; ++q) {  // 16 columns = one 32-byte sector per store
           uint32_t w8[8];
@@ -685,15 +692,16 @@ __global__ void __launch_bounds__(320, 1) keyglobal_kernel(const __grid_constant
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hk = blockIdx.y, b = blockIdx.z;
   const int W = p.W, S = p.S, R = p.R;
-  const int n_units = (S + kUnit - 1) / kUnit;
-  const int Spad = ((S + kTile - 1) / kTile) * kTile;
+  const int q_lo = p.q_lo, q_hi = p.q_hi;
+  const int n_units = (q_hi - q_lo + kUnit - 1) / kUnit;  // 64-query units from q_lo
+  const int Spad = p.q_pad;
   const int groups = p.kv_groups;
 
   // global-row tile and this split's 64-query units [t_lo, t_hi) (per group head)
   const int gt = static_cast<int>(blockIdx.x) / p.n_split;
   const int split = static_cast<int>(blockIdx.x) % p.n_split;
   const int k0 = gt * kTile;
-  const int tmin = first_query_seeing(k0, S, W, R) / kUnit;
+  const int tmin = min(max(first_query_seeing(k0, S, W, R) - q_lo, 0) / kUnit, n_units);
   const int tot = n_units - tmin;
   const int t_lo = tmin + static_cast<int>((static_cast<int64_t>(tot) * split) / p.n_split);
   const int t_hi = tmin + static_cast<int>((static_cast<int64_t>(tot) * (split + 1)) / p.n_split);
@@ -732,9 +740,9 @@ __global__ void __launch_bounds__(320, 1) keyglobal_kernel(const __grid_constant
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  auto unit = [&](int u, int& h, int& q0) {
+  auto unit = [&](int u, int& h, int& q0) {  // q0: absolute position of the unit's first query
     h = hk * groups + u / nT;
-    q0 = (t_lo + u % nT) * kUnit;
+    q0 = q_lo + (t_lo + u % nT) * kUnit;
   };
 
   if (warp == 0) {
@@ -753,10 +761,10 @@ __global__ void __launch_bounds__(320, 1) keyglobal_kernel(const __grid_constant
         const uint32_t qd = sbase + C::OFF_Q + st * 2 * C::UB;
         mbar_expect_tx(BAR(C::B_QFULL + st), 2 * C::UB + 2 * kUnit * 4);
         for (int c = 0; c < D / 64; ++c) {
-          tma_load_4d(qd + c * kUnit * 128, &p.tm_q, BAR(C::B_QFULL + st), c * 64, q0, h, b);
-          tma_load_4d(qd + C::UB + c * kUnit * 128, &p.tm_do, BAR(C::B_QFULL + st), c * 64, q0, h, b);
+          tma_load_4d(qd + c * kUnit * 128, &p.tm_q, BAR(C::B_QFULL + st), c * 64, q0 - q_lo, h, b);
+          tma_load_4d(qd + C::UB + c * kUnit * 128, &p.tm_do, BAR(C::B_QFULL + st), c * 64, q0 - q_lo, h, b);
         }
-        const int64_t li = (static_cast<int64_t>(b) * p.H + h) * Spad + q0;
+        const int64_t li = (static_cast<int64_t>(b) * p.H + h) * Spad + (q0 - q_lo);
         const uint32_t ld = sbase + C::OFF_LSE + st * 2 * kUnit * 4;
         bulk_load(ld, p.lse + li, kUnit * 4, BAR(C::B_QFULL + st));
         bulk_load(ld + kUnit * 4, p.delta + li, kUnit * 4, BAR(C::B_QFULL + st));
@@ -834,7 +842,7 @@ __global__ void __launch_bounds__(320, 1) keyglobal_kernel(const __grid_constant
     const uint32_t lane_off = static_cast<uint32_t>(r & ~31) << 16;
     const float sl2 = p.scale_log2;
     // queries that see this global row: [qa, S)
-    const int qa = kj < p.NG ? first_query_seeing(kj, S, W, R) : S, qb = S;
+    const int qa = kj < p.NG ? first_query_seeing(kj, S, W, R) : S, qb = q_hi;
     const uint32_t scol = tmem + lane_off + 128 * w;
     bool ok = true;
     for (int u = w; u < nU; u += 2) {
@@ -876,7 +884,7 @@ __global__ void __launch_bounds__(320, 1) keyglobal_kernel(const __grid_constant
       tc_fence_before();
       mbar_arrive(BAR(C::B_PFULL + w));
       if constexpr (FUSED) {
-        float* acc = p.dq_acc + ((static_cast<int64_t>(b) * p.H + h) * Spad + q0) * D + r;
+        float* acc = p.dq_acc + ((static_cast<int64_t>(b) * p.H + h) * Spad + (q0 - q_lo)) * D + r;
         if (!drain_dqt(scol, BAR(C::B_DQFULL + w), (u >> 1) & 1, BAR(C::B_DQFREE + w), acc, D, ab)) {
           ok = false;
           break;
@@ -956,20 +964,25 @@ struct KeyLocalCfg {
 
 // Local key tile t of the persistent walk and the 64-query units it meets.
 struct KeyLocalTile {
-  int k0, hk, b, t_lo, nT, nU;
-  __device__ __forceinline__ KeyLocalTile(int t, int n_ktiles, int Hkv, int S, int W, int groups) {
+  int k0, hk, b, t_lo, nT, nU, q_lo;
+  // Key tiles start at k_lo (128 keys each); queries [q_lo, q_hi) in 64-query
+  // units from q_lo.  Every key of [k_lo, q_hi) has a query in range.
+  __device__ __forceinline__ KeyLocalTile(int t, int n_ktiles, int Hkv, int k_lo, int q_lo_, int q_hi, int W,
+                                          int groups)
+      : q_lo(q_lo_) {
     const int kt = t % n_ktiles;
     hk = (t / n_ktiles) % Hkv;
     b = t / (n_ktiles * Hkv);
-    k0 = (n_ktiles - 1 - kt) * kTile;
-    const int qlast = min(k0 + kTile - 1 + W - 1, S - 1);
-    t_lo = k0 / kUnit;
-    nT = qlast / kUnit + 1 - t_lo;
+    k0 = k_lo + (n_ktiles - 1 - kt) * kTile;
+    const int qfirst = max(k0, q_lo), qlast = min(k0 + kTile - 1 + W - 1, q_hi - 1);
+    t_lo = (qfirst - q_lo) / kUnit;
+    nT = (qlast - q_lo) / kUnit + 1 - t_lo;
     nU = nT * groups;
   }
+  // unit ul: head h, absolute position q0 of its first query
   __device__ __forceinline__ void unit(int ul, int groups, int& h, int& q0) const {
     h = hk * groups + ul / nT;
-    q0 = (t_lo + ul % nT) * kUnit;
+    q0 = q_lo + (t_lo + ul % nT) * kUnit;
   }
 };
 
@@ -987,7 +1000,8 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
   uint8_t* smem = align1024(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int W = p.W, S = p.S, R = p.R;
-  const int Spad = ((S + kTile - 1) / kTile) * kTile;
+  const int Spad = p.q_pad;
+  (void)S;
   const int groups = p.kv_groups;
   const int Hkv = p.H / groups;
   const int n_tiles = p.n_ktiles * Hkv * p.B;
@@ -1032,16 +1046,21 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
       int e = 0, nkv = 0;  // Q/dO units issued, K/V tiles issued
       bool ok = true;
       for (int t = blockIdx.x, i = 0; ok && t < n_tiles; t += gridDim.x, ++i) {
-        const KeyLocalTile tl(t, p.n_ktiles, Hkv, S, W, groups);
+        const KeyLocalTile tl(t, p.n_ktiles, Hkv, p.k_lo, p.q_lo, p.q_hi, W, groups);
         const int kb = i & 1;
         PROF_T(tk);
         if (i >= 2 && !mbar_wait(BAR(C::B_KVEMPTY + kb), ((i >> 1) - 1) & 1, ab)) break;
         PROF_ADD(0, tk);
         mbar_expect_tx(BAR(C::B_KVFULL + kb), 2 * C::TB);
         const uint32_t kd = sbase + C::OFF_KV + 2 * kb * C::TB;
+        // tiles that start below this shard's own K / V rows come from the edge copy
+        const bool edge = p.has_edge && tl.k0 < p.kv_main;
+        const int krow = edge ? tl.k0 - p.edge_begin : tl.k0 - p.kv_main;
         for (int c = 0; c < D / 64; ++c) {
-          tma_load_4d(kd + c * kTile * 128, &p.tm_k, BAR(C::B_KVFULL + kb), c * 64, tl.k0, tl.hk, tl.b);
-          tma_load_4d(kd + C::TB + c * kTile * 128, &p.tm_v, BAR(C::B_KVFULL + kb), c * 64, tl.k0, tl.hk, tl.b);
+          tma_load_4d(kd + c * kTile * 128, edge ? &p.tm_ke : &p.tm_k, BAR(C::B_KVFULL + kb), c * 64, krow, tl.hk,
+                      tl.b);
+          tma_load_4d(kd + C::TB + c * kTile * 128, edge ? &p.tm_ve : &p.tm_v, BAR(C::B_KVFULL + kb), c * 64, krow,
+                      tl.hk, tl.b);
         }
         ++nkv;
         for (int ul = 0; ul < tl.nU; ++ul, ++e) {
@@ -1054,10 +1073,10 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
           const uint32_t qd = sbase + C::OFF_Q + st * 2 * C::UB;
           mbar_expect_tx(BAR(C::B_QFULL + st), 2 * C::UB + 2 * kUnit * 4);
           for (int c = 0; c < D / 64; ++c) {
-            tma_load_4d(qd + c * kUnit * 128, &p.tm_q, BAR(C::B_QFULL + st), c * 64, q0, h, tl.b);
-            tma_load_4d(qd + C::UB + c * kUnit * 128, &p.tm_do, BAR(C::B_QFULL + st), c * 64, q0, h, tl.b);
+            tma_load_4d(qd + c * kUnit * 128, &p.tm_q, BAR(C::B_QFULL + st), c * 64, q0 - p.q_lo, h, tl.b);
+            tma_load_4d(qd + C::UB + c * kUnit * 128, &p.tm_do, BAR(C::B_QFULL + st), c * 64, q0 - p.q_lo, h, tl.b);
           }
-          const int64_t li = (static_cast<int64_t>(tl.b) * p.H + h) * Spad + q0;
+          const int64_t li = (static_cast<int64_t>(tl.b) * p.H + h) * Spad + (q0 - p.q_lo);
           const uint32_t ld = sbase + C::OFF_LSE + st * 2 * kUnit * 4;
           bulk_load(ld, p.lse + li, kUnit * 4, BAR(C::B_QFULL + st));
           bulk_load(ld + kUnit * 4, p.delta + li, kUnit * 4, BAR(C::B_QFULL + st));
@@ -1106,7 +1125,7 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
     int u = 0, pit = -1;
     bool pfirst = false;
     for (int t = blockIdx.x, i = 0; ok && t < n_tiles; t += gridDim.x, ++i) {
-      const KeyLocalTile tl(t, p.n_ktiles, Hkv, S, W, groups);
+      const KeyLocalTile tl(t, p.n_ktiles, Hkv, p.k_lo, p.q_lo, p.q_hi, W, groups);
       const int kb = i & 1;
       PROF_T(tk);
       if (!warp_wait(BAR(C::B_KVFULL + kb), (i >> 1) & 1, ab)) { ok = false; break; }
@@ -1156,10 +1175,10 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
     bool ok = true;
     int u = 0;
     for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x) {
-      const KeyLocalTile tl(t, p.n_ktiles, Hkv, S, W, groups);
+      const KeyLocalTile tl(t, p.n_ktiles, Hkv, p.k_lo, p.q_lo, p.q_hi, W, groups);
       const int kj = tl.k0 + r;
       // queries that see this key row: [qa, qb)
-      const int qa = kj, qb = kj < S ? min(kj + W, S) : kj;
+      const int qa = kj, qb = kj < p.q_hi ? min(kj + W, p.q_hi) : kj;
       for (int ul = 0; ul < tl.nU; ++ul) {
         const int uu = u++;
         if ((uu & 1) != w) continue;
@@ -1202,7 +1221,7 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
         tc_fence_before();
         mbar_arrive(BAR(C::B_PFULL + w));
         if constexpr (FUSED) {
-          float* acc = p.dq_acc + ((static_cast<int64_t>(tl.b) * p.H + h) * Spad + q0) * D + r;
+          float* acc = p.dq_acc + ((static_cast<int64_t>(tl.b) * p.H + h) * Spad + (q0 - p.q_lo)) * D + r;
           if (!drain_dqt(scol, BAR(C::B_DQFULL + w), (uu >> 1) & 1, BAR(C::B_DQFREE + w), acc, D, ab)) {
             ok = false;
             break;
@@ -1225,16 +1244,17 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
     const int r = ((warp & 3) << 5) | lane;
     const uint32_t lane_off = static_cast<uint32_t>(r & ~31) << 16;
     for (int t = blockIdx.x, i = 0; t < n_tiles; t += gridDim.x, ++i) {
-      const KeyLocalTile tl(t, p.n_ktiles, Hkv, S, W, groups);
+      const KeyLocalTile tl(t, p.n_ktiles, Hkv, p.k_lo, p.q_lo, p.q_hi, W, groups);
       const int kj = tl.k0 + r;
-      const bool row_ok = kj < S;
+      const bool row_ok = kj < p.q_hi;
+      const bool halo = kj < p.kv_main;  // key of the previous shard: output to dkh / dvh, no fold-in
       // global rows of this key position (looked up before the wait)
       const int blk = kj / W;
       const int64_t gbase = (static_cast<int64_t>(tl.b) * Hkv + tl.hk) * static_cast<int64_t>(p.NG);
       int grow[5];
       float gsc[5];
       int ng = 0;
-      if (row_ok) {
+      if (row_ok && !halo) {
         if (kj == blk * W) {
           grow[ng] = blk * R;
           gsc[ng] = 1.f;
@@ -1252,8 +1272,14 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
             }
         }
       }
-      T* const dkrow = reinterpret_cast<T*>(p.dk) + tl.b * p.dk_sb + tl.hk * p.dk_sh + static_cast<int64_t>(kj) * p.dk_ss;
-      T* const dvrow = reinterpret_cast<T*>(p.dv) + tl.b * p.dv_sb + tl.hk * p.dv_sh + static_cast<int64_t>(kj) * p.dv_ss;
+      T* const dkrow =
+          halo ? reinterpret_cast<T*>(p.dkh) + tl.b * p.dkh_sb + tl.hk * p.dkh_sh + static_cast<int64_t>(kj - p.k_lo) * p.dkh_ss
+               : reinterpret_cast<T*>(p.dk) + tl.b * p.dk_sb + tl.hk * p.dk_sh +
+                     static_cast<int64_t>(kj - p.kv_main) * p.dk_ss;
+      T* const dvrow =
+          halo ? reinterpret_cast<T*>(p.dvh) + tl.b * p.dvh_sb + tl.hk * p.dvh_sh + static_cast<int64_t>(kj - p.k_lo) * p.dvh_ss
+               : reinterpret_cast<T*>(p.dv) + tl.b * p.dv_sb + tl.hk * p.dv_sh +
+                     static_cast<int64_t>(kj - p.kv_main) * p.dv_ss;
       PROF_T(te);
       if (!mbar_wait(BAR(C::B_ACCFULL), i & 1, ab)) break;
       PROF_ADD(16, te);
@@ -1311,9 +1337,9 @@ __global__ void __launch_bounds__(448, 1) keylocal_kernel(const __grid_constant_
         for (int which = 0; which < 2; ++which) {
           const float* dg = which == 0 ? p.dgk : p.dgv;
           T* drow = which == 0 ? reinterpret_cast<T*>(p.dk) + tl.b * p.dk_sb + tl.hk * p.dk_sh +
-                                     static_cast<int64_t>(kj_s) * p.dk_ss
+                                     static_cast<int64_t>(kj_s - p.kv_main) * p.dk_ss
                                : reinterpret_cast<T*>(p.dv) + tl.b * p.dv_sb + tl.hk * p.dv_sh +
-                                     static_cast<int64_t>(kj_s) * p.dv_ss;
+                                     static_cast<int64_t>(kj_s - p.kv_main) * p.dv_ss;
           float a[CPL];
           if constexpr (CPL == 4) {
             const uint2 cur = *reinterpret_cast<const uint2*>(drow + c0);
@@ -1458,7 +1484,7 @@ static cudaError_t launch_key_passes(BwdLaunch& L, cudaStream_t st, Mark& mark, 
   const KeyPassParams& gp = L.global;
   const int Hkv = gp.H / gp.kv_groups;
   const int n_gtiles = (gp.NG + kTile - 1) / kTile;
-  {
+  if (L.phase != 2) {
     using C = KeyCfg<D, FUSED>;
     auto kern = keyglobal_kernel<D, BF16, FUSED>;
     if ((e = set_smem(kern, C::SMEM)) != cudaSuccess) return e;
@@ -1466,7 +1492,7 @@ static cudaError_t launch_key_passes(BwdLaunch& L, cudaStream_t st, Mark& mark, 
     kern<<<dim3(n_gtiles * gp.n_split, Hkv, B), 320, C::SMEM, st>>>(gp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
-  {
+  if (L.phase != 2) {
     const int64_t n4 = static_cast<int64_t>(B) * Hkv * gp.NG * D / 4;
     const int64_t nb = (n4 + 255) / 256;
     if ((e = mark(2)) != cudaSuccess) return e;
@@ -1475,6 +1501,7 @@ static cudaError_t launch_key_passes(BwdLaunch& L, cudaStream_t st, Mark& mark, 
         reinterpret_cast<float4*>(L.dgk), reinterpret_cast<float4*>(L.dgv));
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
+  if (L.phase == 1) return done();  // shard: dG goes through a cross-GPU sum first
   if (L.d_alpha && gp.R > 1) {
     if ((e = mark(3)) != cudaSuccess) return e;
     dalpha_kernel<BF16><<<Hkv, 256, 0, st>>>(L.dgk, L.dgv, L.gk_rows, L.gv_rows, B, Hkv, gp.NG, gp.R, D, L.d_alpha);
@@ -1511,7 +1538,7 @@ template <int D, bool BF16>
 static cudaError_t launch_bwd_t(const BwdLaunch& L_, cudaStream_t st) {
   BwdLaunch& L = const_cast<BwdLaunch&>(L_);
   const QueryPassParams& qp = L.qp;
-  const int B = qp.B, H = qp.H, S = qp.S;
+  const int B = qp.B, H = qp.H;
   const int Spad = qp.n_qtiles * kTile;
   cudaError_t e;
   int nk = 0;
@@ -1526,12 +1553,12 @@ static cudaError_t launch_bwd_t(const BwdLaunch& L_, cudaStream_t st) {
     L.n_kernels = nk;
     return L.events ? cudaEventRecord(L.events[nk], st) : cudaSuccess;
   };
-  {
+  if (L.phase != 2) {
     constexpr int RPB = 8 * (32 / (D / 8));  // rows per 256-thread block
     dim3 grid((Spad + RPB - 1) / RPB, B * H);
     if ((e = mark(0)) != cudaSuccess) return e;
     delta_kernel<D, BF16><<<grid, 256, 0, st>>>(L.o, L.d_o, L.o_st[0], L.o_st[1], L.o_st[2], L.do_st[0], L.do_st[1],
-                                                L.do_st[2], L.lse_in, H, S, Spad, L.lse2, L.delta,
+                                                L.do_st[2], L.lse_in, H, qp.q_len, Spad, L.lse2, L.delta,
                                                 L.fused ? L.global.dq_acc : nullptr);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }

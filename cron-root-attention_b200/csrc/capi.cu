@@ -166,10 +166,12 @@ int global_splits(int batch, int kv_heads, int seq_len, int NG) {
   return static_cast<int>(s);
 }
 
-BwdLayout bwd_layout(int batch, int heads, int kv_heads, int seq_len, int head_dim, int use_relay, int top_k) {
+// q_len: query rows of this GPU (a sequence shard), or the whole sequence (-1).
+BwdLayout bwd_layout(int batch, int heads, int kv_heads, int seq_len, int head_dim, int use_relay, int top_k,
+                     int q_len = -1) {
   BwdLayout L;
   const int64_t NG = cra_global_rows(seq_len, use_relay, top_k);
-  const int64_t Spad = static_cast<int64_t>((seq_len + kTile - 1) / kTile) * kTile;
+  const int64_t Spad = static_cast<int64_t>(((q_len < 0 ? seq_len : q_len) + kTile - 1) / kTile) * kTile;
   L.n_split = global_splits(batch, kv_heads, seq_len, static_cast<int>(NG));
   const size_t rowsz = round256(sizeof(float) * batch * heads * Spad);
   const size_t gsz = round256(sizeof(float) * batch * kv_heads * NG * head_dim);
@@ -319,6 +321,27 @@ namespace {
 
 // cra_bwd's body; with `events` non-null (BwdLaunch::kMaxKernels + 1 of
 // them) an event is recorded before each kernel and after the last.
+// One GPU's shard of a sequence split across GPUs (backward).  phase 1:
+// delta, global-row pass and reduce (dG of this shard's queries into dg_k /
+// dg_v); phase 2: local key pass (with the summed dG folded in) and dQ.
+struct ShardSpec {
+  int phase;
+  int64_t q_begin;
+  int q_len;
+  const void* k_edge;
+  const void* v_edge;
+  const int64_t* ke_strides;
+  const int64_t* ve_strides;
+  int64_t edge_begin;
+  int edge_len;
+  void* dk_halo;
+  void* dv_halo;
+  const int64_t* dkh_strides;
+  const int64_t* dvh_strides;
+  float* dg_k;
+  float* dg_v;
+};
+
 int bwd_impl(const void* q, const void* k, const void* v, const void* o, const void* d_o, const float* lse,
              const void* g_k, const void* g_v, const int32_t* g_src, const int64_t* q_strides,
              const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides, const int64_t* do_strides,
@@ -326,23 +349,30 @@ int bwd_impl(const void* q, const void* k, const void* v, const void* o, const v
              float softmax_scale, const float* relay_log_scale, void* dq, void* dk, void* dv,
              const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
              float* d_relay_log_scale, void* workspace, size_t workspace_bytes, int* dev_error, void* stream,
-             cudaEvent_t* events, int* n_kernels, int* kernel_ids, int fused_req) {
-  const bool fused = fused_req && head_dim == 128;
+             cudaEvent_t* events, int* n_kernels, int* kernel_ids, int fused_req, const ShardSpec* sh = nullptr) {
+  const bool fused = fused_req && head_dim == 128 && !sh;
+  const int phase = sh ? sh->phase : 0;
+  // query rows held by the q / o / d_o / dq / lse tensors, and their first position
+  const int q_len = sh ? sh->q_len : seq_len;
+  const int q_begin = sh ? static_cast<int>(sh->q_begin) : 0;
   CRA_TRY(check_common(batch, heads, kv_heads, seq_len, head_dim, dtype, top_k));
   CRA_TRY(check_tensor("q", q, q_strides, batch, heads));
-  CRA_TRY(check_tensor("k", k, k_strides, batch, kv_heads));
-  CRA_TRY(check_tensor("v", v, v_strides, batch, kv_heads));
-  CRA_TRY(check_tensor("o", o, o_strides, batch, heads));
   CRA_TRY(check_tensor("d_o", d_o, do_strides, batch, heads));
-  CRA_TRY(check_tensor("dq", dq, dq_strides, batch, heads));
-  CRA_TRY(check_tensor("dk", dk, dk_strides, batch, kv_heads));
-  CRA_TRY(check_tensor("dv", dv, dv_strides, batch, kv_heads));
-  if (!lse || !g_k || !g_v) return fail(CRA_ERR_INVALID_ARGUMENT, "lse / g_k / g_v: null pointer");
-  if (use_relay && !g_src) return fail(CRA_ERR_INVALID_ARGUMENT, "g_src: null with the relay active");
+  if (phase != 2) CRA_TRY(check_tensor("o", o, o_strides, batch, heads));
+  if (phase != 1) {
+    CRA_TRY(check_tensor("k", k, k_strides, batch, kv_heads));
+    CRA_TRY(check_tensor("v", v, v_strides, batch, kv_heads));
+    CRA_TRY(check_tensor("dq", dq, dq_strides, batch, heads));
+    CRA_TRY(check_tensor("dk", dk, dk_strides, batch, kv_heads));
+    CRA_TRY(check_tensor("dv", dv, dv_strides, batch, kv_heads));
+  }
+  if (!g_k || !g_v) return fail(CRA_ERR_INVALID_ARGUMENT, "g_k / g_v: null pointer");
+  if (phase != 2 && !lse) return fail(CRA_ERR_INVALID_ARGUMENT, "lse: null pointer");
+  if (phase != 1 && use_relay && !g_src) return fail(CRA_ERR_INVALID_ARGUMENT, "g_src: null with the relay active");
   if (!aligned16(g_k) || !aligned16(g_v)) return fail(CRA_ERR_MISALIGNED, "g_k / g_v: not 16-byte aligned");
   if (!(softmax_scale > 0.f) || !std::isfinite(softmax_scale))
     return fail(CRA_ERR_INVALID_ARGUMENT, "softmax_scale must be finite and > 0");
-  const BwdLayout lay = bwd_layout(batch, heads, kv_heads, seq_len, head_dim, use_relay, top_k);
+  const BwdLayout lay = bwd_layout(batch, heads, kv_heads, seq_len, head_dim, use_relay, top_k, q_len);
   const size_t need = fused ? lay.total_fused : lay.total;
   if (!workspace || workspace_bytes < need)
     return fail(CRA_ERR_WORKSPACE, "workspace: %zu bytes given, %zu needed", workspace_bytes, need);
@@ -362,24 +392,45 @@ int bwd_impl(const void* q, const void* k, const void* v, const void* o, const v
   float* lse2 = reinterpret_cast<float*>(ws + lay.off_lse2);
   float* delta = reinterpret_cast<float*>(ws + lay.off_delta);
   QueryPassParams& qp = L.qp;
-  CRA_TRY(make_tmap("q", &qp.tm_q, q, bf16, head_dim, seq_len, heads, batch, q_strides));
-  CRA_TRY(make_tmap("k", &qp.tm_k, k, bf16, head_dim, seq_len, kv_heads, batch, k_strides, kUnit));
-  CRA_TRY(make_tmap("v", &qp.tm_v, v, bf16, head_dim, seq_len, kv_heads, batch, v_strides, kUnit));
+  CRA_TRY(make_tmap("q", &qp.tm_q, q, bf16, head_dim, q_len, heads, batch, q_strides));
   CRA_TRY(make_tmap("g_k", &qp.tm_gk, g_k, bf16, head_dim, NG, kv_heads, batch, g_st, kUnit));
   CRA_TRY(make_tmap("g_v", &qp.tm_gv, g_v, bf16, head_dim, NG, kv_heads, batch, g_st, kUnit));
-  CRA_TRY(make_tmap("d_o", &qp.tm_do, d_o, bf16, head_dim, seq_len, heads, batch, do_strides));
-  CUtensorMap tm_q64, tm_do64, tm_k128, tm_v128, tm_gk128, tm_gv128;
-  CRA_TRY(make_tmap("q", &tm_q64, q, bf16, head_dim, seq_len, heads, batch, q_strides, kUnit));
-  CRA_TRY(make_tmap("d_o", &tm_do64, d_o, bf16, head_dim, seq_len, heads, batch, do_strides, kUnit));
-  CRA_TRY(make_tmap("k", &tm_k128, k, bf16, head_dim, seq_len, kv_heads, batch, k_strides));
-  CRA_TRY(make_tmap("v", &tm_v128, v, bf16, head_dim, seq_len, kv_heads, batch, v_strides));
+  CRA_TRY(make_tmap("d_o", &qp.tm_do, d_o, bf16, head_dim, q_len, heads, batch, do_strides));
+  CUtensorMap tm_q64, tm_do64, tm_k128, tm_v128, tm_gk128, tm_gv128, tm_ke128, tm_ve128;
+  CRA_TRY(make_tmap("q", &tm_q64, q, bf16, head_dim, q_len, heads, batch, q_strides, kUnit));
+  CRA_TRY(make_tmap("d_o", &tm_do64, d_o, bf16, head_dim, q_len, heads, batch, do_strides, kUnit));
   CRA_TRY(make_tmap("g_k", &tm_gk128, g_k, bf16, head_dim, NG, kv_heads, batch, g_st));
   CRA_TRY(make_tmap("g_v", &tm_gv128, g_v, bf16, head_dim, NG, kv_heads, batch, g_st));
+  if (phase != 1) {
+    CRA_TRY(make_tmap("k", &qp.tm_k, k, bf16, head_dim, q_len, kv_heads, batch, k_strides, kUnit));
+    CRA_TRY(make_tmap("v", &qp.tm_v, v, bf16, head_dim, q_len, kv_heads, batch, v_strides, kUnit));
+    CRA_TRY(make_tmap("k", &tm_k128, k, bf16, head_dim, q_len, kv_heads, batch, k_strides));
+    CRA_TRY(make_tmap("v", &tm_v128, v, bf16, head_dim, q_len, kv_heads, batch, v_strides));
+  }
+  const bool edge = sh && sh->k_edge;
+  if (edge && phase == 2) {
+    CRA_TRY(make_tmap("k_edge", &qp.tm_ke, sh->k_edge, bf16, head_dim, sh->edge_len, kv_heads, batch, sh->ke_strides,
+                      kUnit));
+    CRA_TRY(make_tmap("v_edge", &qp.tm_ve, sh->v_edge, bf16, head_dim, sh->edge_len, kv_heads, batch, sh->ve_strides,
+                      kUnit));
+    CRA_TRY(make_tmap("k_edge", &tm_ke128, sh->k_edge, bf16, head_dim, sh->edge_len, kv_heads, batch,
+                      sh->ke_strides));
+    CRA_TRY(make_tmap("v_edge", &tm_ve128, sh->v_edge, bf16, head_dim, sh->edge_len, kv_heads, batch,
+                      sh->ve_strides));
+    qp.has_edge = 1;
+    qp.edge_begin = static_cast<int>(sh->edge_begin);
+  }
+  const int k_lo = q_begin - (W - 1) > 0 ? q_begin - (W - 1) : 0;  // first key a shard query sees
+  static const int64_t kNoStrides[3] = {0, 0, 0};  // tensors a shard phase does not touch
+  if (!dq_strides) dq_strides = kNoStrides;
+  if (!dk_strides) dk_strides = kNoStrides;
+  if (!dv_strides) dv_strides = kNoStrides;
+  if (!o_strides) o_strides = kNoStrides;
   qp.out = dq;
   qp.out_sb = dq_strides[0];
   qp.out_sh = dq_strides[1];
   qp.out_ss = dq_strides[2];
-  qp.out_v8 = rows_aligned32(dq, dq_strides, batch, heads, seq_len);
+  qp.out_v8 = phase != 1 && rows_aligned32(dq, dq_strides, batch, heads, q_len);
   qp.lse = lse2;
   qp.delta = delta;
   qp.B = batch;
@@ -389,10 +440,10 @@ int bwd_impl(const void* q, const void* k, const void* v, const void* o, const v
   qp.W = W;
   qp.R = R;
   qp.NG = NG;
-  qp.n_qtiles = (seq_len + kTile - 1) / kTile;
-  qp.q_begin = 0;
-  qp.q_len = seq_len;
-  qp.kv_begin = 0;
+  qp.n_qtiles = (q_len + kTile - 1) / kTile;
+  qp.q_begin = q_begin;
+  qp.q_len = q_len;
+  qp.kv_begin = q_begin;
   qp.scale = softmax_scale;
   qp.scale_log2 = softmax_scale * 1.4426950408889634f;
   qp.err = dev_error;
@@ -402,6 +453,27 @@ int bwd_impl(const void* q, const void* k, const void* v, const void* o, const v
     kp.tm_do = tm_do64;
     kp.tm_k = mode ? tm_k128 : tm_gk128;
     kp.tm_v = mode ? tm_v128 : tm_gv128;
+    kp.q_lo = q_begin;
+    kp.q_hi = q_begin + q_len;
+    kp.q_pad = qp.n_qtiles * kTile;
+    kp.k_lo = sh ? k_lo : 0;
+    kp.kv_main = q_begin;
+    if (mode && edge) {
+      kp.has_edge = 1;
+      kp.edge_begin = static_cast<int>(sh->edge_begin);
+      kp.tm_ke = tm_ke128;
+      kp.tm_ve = tm_ve128;
+    }
+    if (sh && sh->dk_halo) {
+      kp.dkh = sh->dk_halo;
+      kp.dvh = sh->dv_halo;
+      kp.dkh_sb = sh->dkh_strides[0];
+      kp.dkh_sh = sh->dkh_strides[1];
+      kp.dkh_ss = sh->dkh_strides[2];
+      kp.dvh_sb = sh->dvh_strides[0];
+      kp.dvh_sh = sh->dvh_strides[1];
+      kp.dvh_ss = sh->dvh_strides[2];
+    }
     kp.lse = lse2;
     kp.delta = delta;
     kp.dk = dk;
@@ -412,10 +484,13 @@ int bwd_impl(const void* q, const void* k, const void* v, const void* o, const v
     kp.dv_sb = dv_strides[0];
     kp.dv_sh = dv_strides[1];
     kp.dv_ss = dv_strides[2];
-    kp.dkv_v8 = rows_aligned32(dk, dk_strides, batch, kv_heads, seq_len) &&
-                rows_aligned32(dv, dv_strides, batch, kv_heads, seq_len);
-    kp.dgk = reinterpret_cast<float*>(ws + lay.off_dgk);
-    kp.dgv = reinterpret_cast<float*>(ws + lay.off_dgv);
+    kp.dkv_v8 = phase != 1 && rows_aligned32(dk, dk_strides, batch, kv_heads, q_len) &&
+                rows_aligned32(dv, dv_strides, batch, kv_heads, q_len) &&
+                (!sh || !sh->dk_halo ||
+                 (rows_aligned32(sh->dk_halo, sh->dkh_strides, batch, kv_heads, W - 1) &&
+                  rows_aligned32(sh->dv_halo, sh->dvh_strides, batch, kv_heads, W - 1)));
+    kp.dgk = sh ? sh->dg_k : reinterpret_cast<float*>(ws + lay.off_dgk);
+    kp.dgv = sh ? sh->dg_v : reinterpret_cast<float*>(ws + lay.off_dgv);
     kp.gsrc = g_src;
     kp.relay_scale = use_relay ? relay_log_scale : nullptr;
     kp.part_k = reinterpret_cast<float*>(ws + lay.off_pk);
@@ -430,7 +505,7 @@ int bwd_impl(const void* q, const void* k, const void* v, const void* o, const v
     kp.NB = NB;
     kp.NG = NG;
     kp.top_k = top_k;
-    kp.n_ktiles = (seq_len + kTile - 1) / kTile;
+    kp.n_ktiles = (q_begin + q_len - (sh ? k_lo : 0) + kTile - 1) / kTile;
     kp.n_split = lay.n_split;
     kp.scale = softmax_scale;
     kp.scale_log2 = qp.scale_log2;
@@ -445,8 +520,9 @@ int bwd_impl(const void* q, const void* k, const void* v, const void* o, const v
   L.lse_in = lse;
   L.lse2 = lse2;
   L.delta = delta;
-  L.dgk = reinterpret_cast<float*>(ws + lay.off_dgk);
-  L.dgv = reinterpret_cast<float*>(ws + lay.off_dgv);
+  L.dgk = sh ? sh->dg_k : reinterpret_cast<float*>(ws + lay.off_dgk);
+  L.dgv = sh ? sh->dg_v : reinterpret_cast<float*>(ws + lay.off_dgv);
+  L.phase = phase;
   L.d_alpha = (use_relay && relay_log_scale) ? d_relay_log_scale : nullptr;
   L.gk_rows = g_k;
   L.gv_rows = g_v;
@@ -779,6 +855,99 @@ int cra_fwd_varlen(const void* q, const void* k, const void* v, const void* g_k,
   p.err = dev_error;
   cudaError_t e = launch_fwd(p, head_dim, bf16, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? CRA_OK : fail(CRA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+}
+
+}  // extern "C"
+
+extern "C" {
+
+size_t cra_bwd_shard_workspace_bytes(int batch, int heads, int kv_heads, int64_t seq_len, int q_len, int head_dim,
+                                     int use_relay, int top_k) {
+  if (seq_len < 1 || seq_len > INT32_MAX || q_len < 1) return 0;
+  if (check_common(batch, heads, kv_heads, static_cast<int>(seq_len), head_dim, CRA_BF16, top_k) != CRA_OK) return 0;
+  return bwd_layout(batch, heads, kv_heads, static_cast<int>(seq_len), head_dim, use_relay, top_k, q_len).total;
+}
+
+namespace {
+int check_shard(int64_t seq_len, int64_t q_begin, int q_len) {
+  if (seq_len < 1 || seq_len > INT32_MAX) return fail(CRA_ERR_INVALID_ARGUMENT, "seq_len out of range");
+  const int W = cra_window(seq_len);
+  if (q_begin < 0 || q_len < 1 || q_begin + q_len > seq_len || q_begin % W != 0)
+    return fail(CRA_ERR_INVALID_ARGUMENT, "query shard [%lld, %lld) must start on a multiple of W = %d inside the sequence",
+                static_cast<long long>(q_begin), static_cast<long long>(q_begin + q_len), W);
+  return CRA_OK;
+}
+}  // namespace
+
+int cra_bwd_shard_global(const void* q, const void* o, const void* d_o, const float* lse, const void* g_k,
+                         const void* g_v, const int64_t* q_strides, const int64_t* o_strides,
+                         const int64_t* do_strides, int batch, int heads, int kv_heads, int64_t seq_len,
+                         int64_t q_begin, int q_len, int head_dim, int dtype, int use_relay, int top_k,
+                         float softmax_scale, float* dg_k, float* dg_v, void* workspace, size_t workspace_bytes,
+                         int* dev_error, void* stream) {
+  CRA_TRY(check_shard(seq_len, q_begin, q_len));
+  if (!dg_k || !dg_v) return fail(CRA_ERR_INVALID_ARGUMENT, "dg_k / dg_v: null pointer");
+  ShardSpec sh{};
+  sh.phase = 1;
+  sh.q_begin = q_begin;
+  sh.q_len = q_len;
+  sh.dg_k = dg_k;
+  sh.dg_v = dg_v;
+  return bwd_impl(q, nullptr, nullptr, o, d_o, lse, g_k, g_v, nullptr, q_strides, nullptr, nullptr, o_strides,
+                  do_strides, batch, heads, kv_heads, static_cast<int>(seq_len), head_dim, dtype, use_relay, top_k,
+                  softmax_scale, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, workspace,
+                  workspace_bytes, dev_error, stream, nullptr, nullptr, nullptr, 0, &sh);
+}
+
+int cra_bwd_shard_local(const void* q, const void* k, const void* v, const void* d_o, const void* g_k,
+                        const void* g_v, const int32_t* g_src, const int64_t* q_strides, const int64_t* k_strides,
+                        const int64_t* v_strides, const int64_t* do_strides, const void* k_edge, const void* v_edge,
+                        const int64_t* ke_strides, const int64_t* ve_strides, int64_t edge_begin, int edge_len,
+                        int batch, int heads, int kv_heads, int64_t seq_len, int64_t q_begin, int q_len,
+                        int head_dim, int dtype, int use_relay, int top_k, float softmax_scale,
+                        const float* relay_log_scale, const float* dg_k, const float* dg_v, void* dq, void* dk,
+                        void* dv, void* dk_halo, void* dv_halo, const int64_t* dq_strides, const int64_t* dk_strides,
+                        const int64_t* dv_strides, const int64_t* dkh_strides, const int64_t* dvh_strides,
+                        float* d_relay_log_scale, void* workspace, size_t workspace_bytes, int* dev_error,
+                        void* stream) {
+  CRA_TRY(check_shard(seq_len, q_begin, q_len));
+  if (!dg_k || !dg_v) return fail(CRA_ERR_INVALID_ARGUMENT, "dg_k / dg_v: null pointer");
+  const int W = cra_window(seq_len);
+  const int64_t k_lo = q_begin - (W - 1) > 0 ? q_begin - (W - 1) : 0;
+  ShardSpec sh{};
+  sh.phase = 2;
+  sh.q_begin = q_begin;
+  sh.q_len = q_len;
+  sh.dg_k = const_cast<float*>(dg_k);
+  sh.dg_v = const_cast<float*>(dg_v);
+  if (q_begin > 0) {
+    const int64_t need_hi = std::min<int64_t>(q_begin + kTile, q_begin + q_len);
+    if (!k_edge || !v_edge || edge_begin > k_lo || edge_begin + edge_len < need_hi)
+      return fail(CRA_ERR_INVALID_ARGUMENT,
+                  "k_edge / v_edge must cover keys [%lld, %lld) (the halo and the shard's first 128 rows)",
+                  static_cast<long long>(k_lo), static_cast<long long>(need_hi));
+    if (!dk_halo || !dv_halo || !dkh_strides || !dvh_strides)
+      return fail(CRA_ERR_INVALID_ARGUMENT, "dk_halo / dv_halo: null (the shard has a halo of %lld keys)",
+                  static_cast<long long>(q_begin - k_lo));
+    CRA_TRY(check_tensor("k_edge", k_edge, ke_strides, batch, kv_heads));
+    CRA_TRY(check_tensor("v_edge", v_edge, ve_strides, batch, kv_heads));
+    CRA_TRY(check_tensor("dk_halo", dk_halo, dkh_strides, batch, kv_heads));
+    CRA_TRY(check_tensor("dv_halo", dv_halo, dvh_strides, batch, kv_heads));
+    sh.k_edge = k_edge;
+    sh.v_edge = v_edge;
+    sh.ke_strides = ke_strides;
+    sh.ve_strides = ve_strides;
+    sh.edge_begin = edge_begin;
+    sh.edge_len = edge_len;
+    sh.dk_halo = dk_halo;
+    sh.dv_halo = dv_halo;
+    sh.dkh_strides = dkh_strides;
+    sh.dvh_strides = dvh_strides;
+  }
+  return bwd_impl(q, k, v, nullptr, d_o, nullptr, g_k, g_v, g_src, q_strides, k_strides, v_strides, nullptr,
+                  do_strides, batch, heads, kv_heads, static_cast<int>(seq_len), head_dim, dtype, use_relay, top_k,
+                  softmax_scale, relay_log_scale, dq, dk, dv, dq_strides, dk_strides, dv_strides, d_relay_log_scale,
+                  workspace, workspace_bytes, dev_error, stream, nullptr, nullptr, nullptr, 0, &sh);
 }
 
 }  // extern "C"

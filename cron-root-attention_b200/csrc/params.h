@@ -76,6 +76,19 @@ struct alignas(64) KeyPassParams {
   int B, H, kv_groups, S, W, R, NB, NG, top_k;
   int n_ktiles;       // key tiles per (b, hkv)
   int n_split;        // global mode: query splits per key tile
+  // Sequence shard (backward of a sequence split across GPUs).  Positions
+  // are absolute; this GPU's queries are [q_lo, q_hi) (Q / dO / lse / delta
+  // rows hold them from q_lo, q_pad rows per (b, h) in the padded arrays);
+  // local mode walks the keys [k_lo, q_hi) -- the W - 1 halo keys of the
+  // previous shard first -- with K / V rows from kv_main in tm_k / tm_v and,
+  // with has_edge, rows below kv_main + 128 from the edge copy tm_ke / tm_ve
+  // (row 0 = edge_begin); dK / dV of keys below kv_main go to dkh / dvh (row
+  // 0 = k_lo, no global-row fold-in: their blocks belong to the previous
+  // shard).  Whole sequence: q_lo = k_lo = kv_main = 0, q_hi = S.
+  int q_lo, q_hi, q_pad, k_lo, kv_main, has_edge, edge_begin;
+  CUtensorMap tm_ke, tm_ve;
+  void* dkh; void* dvh;
+  int64_t dkh_sb, dkh_sh, dkh_ss, dvh_sb, dvh_sh, dvh_ss;
   float scale, scale_log2;
   int* err;
 };
@@ -99,6 +112,7 @@ struct BwdLaunch {
   // Optional timing: when non-null, events[i] is recorded on the stream just
   // before kernel i and events[n_kernels] after the last one.
   bool fused;              // dQ from the key passes (fp32 atomics), no dQ pass
+  int phase;               // 0 all kernels; shard: 1 delta + global-row pass + reduce, 2 the rest
   static constexpr int kMaxKernels = 8;
   cudaEvent_t* events;
   int n_kernels;                // set by launch_bwd: kernels launched (timed)

@@ -162,6 +162,48 @@ int cra_fwd_varlen(const void* q, const void* k, const void* v, const void* g_k,
                    int top_k, float softmax_scale, void* o, const int64_t* o_strides, float* lse, int* dev_error,
                    void* stream);
 
+/* Backward of one GPU's shard of a sequence split across GPUs, in two
+ * phases around a cross-GPU sum (no counterpart in the reference, which is
+ * single-GPU).  The shard owns queries and keys [q_begin, q_begin + q_len)
+ * (q_begin a multiple of W); q / o / d_o / lse / dq / k / v / dk / dv hold
+ * those rows; g_k / g_v / g_src are the FULL global-row list of the
+ * sequence (as the forward gathered it; g_src absolute positions).
+ *   cra_bwd_shard_global: dG_k / dG_v (fp32 [batch, kv_heads, NG, D],
+ *     overwritten) of every global row from this shard's queries.  The
+ *     caller then sums dg_k / dg_v over all shards (an all-reduce).
+ *   cra_bwd_shard_local (same workspace, after the sum): dq of the shard's
+ *     queries; dk / dv of its keys from its own queries plus the summed dG of
+ *     its blocks' global rows; and dk_halo / dv_halo: the contributions of
+ *     this shard's queries to the previous shard's last W - 1 keys (rows
+ *     from max(q_begin - (W - 1), 0)), which the caller sends to the previous
+ *     shard and adds to its dk / dv.  k_edge / v_edge (edge_len rows from
+ *     absolute position edge_begin) must cover [max(q_begin - (W - 1), 0),
+ *     min(q_begin + 128, q_begin + q_len)): the halo keys plus the shard's
+ *     first rows.  Not needed for the first shard (q_begin = 0).
+ *     d_relay_log_scale (nullable) receives the scale gradient of the summed
+ *     dG: the same on every shard, so exactly one shard should report it.
+ * Workspace: cra_bwd_shard_workspace_bytes() bytes, 256-byte aligned, the
+ * same buffer for both phases. */
+size_t cra_bwd_shard_workspace_bytes(int batch, int heads, int kv_heads, int64_t seq_len, int q_len, int head_dim,
+                                     int use_relay, int top_k);
+int cra_bwd_shard_global(const void* q, const void* o, const void* d_o, const float* lse, const void* g_k,
+                         const void* g_v, const int64_t* q_strides, const int64_t* o_strides,
+                         const int64_t* do_strides, int batch, int heads, int kv_heads, int64_t seq_len,
+                         int64_t q_begin, int q_len, int head_dim, int dtype, int use_relay, int top_k,
+                         float softmax_scale, float* dg_k, float* dg_v, void* workspace, size_t workspace_bytes,
+                         int* dev_error, void* stream);
+int cra_bwd_shard_local(const void* q, const void* k, const void* v, const void* d_o, const void* g_k,
+                        const void* g_v, const int32_t* g_src, const int64_t* q_strides, const int64_t* k_strides,
+                        const int64_t* v_strides, const int64_t* do_strides, const void* k_edge, const void* v_edge,
+                        const int64_t* ke_strides, const int64_t* ve_strides, int64_t edge_begin, int edge_len,
+                        int batch, int heads, int kv_heads, int64_t seq_len, int64_t q_begin, int q_len,
+                        int head_dim, int dtype, int use_relay, int top_k, float softmax_scale,
+                        const float* relay_log_scale, const float* dg_k, const float* dg_v, void* dq, void* dk,
+                        void* dv, void* dk_halo, void* dv_halo, const int64_t* dq_strides, const int64_t* dk_strides,
+                        const int64_t* dv_strides, const int64_t* dkh_strides, const int64_t* dvh_strides,
+                        float* d_relay_log_scale, void* workspace, size_t workspace_bytes, int* dev_error,
+                        void* stream);
+
 /* Bytes of device workspace cra_bwd needs for these sizes (256-byte aligned
  * base required). */
 size_t cra_bwd_workspace_bytes(int batch, int heads, int kv_heads, int seq_len, int head_dim, int use_relay,

@@ -106,3 +106,42 @@ def test_relay_build_shard_rejects_wrong_scale_length():
     k = torch.zeros(1, 2, 3000, 64, dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="relay_log_scale"):
         LibcraShardOps().relay_build_shard(k, k, 3000, 0, True, 2, torch.zeros(3))
+
+
+def _bwd_worker(rank, world, port, S, out_dir):
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    for p in (root, os.path.join(root, "cron-root-attention_b200"), here):
+        sys.path.insert(0, p)
+    import torch.distributed as dist
+    from cron_root_attention.parallel import seq_parallel_attention, seq_shard
+    from shard_oracle import OracleShardOps
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    g = torch.Generator().manual_seed(8)
+    q, k, v, do = (torch.randn(1, 2, S, 16, generator=g, dtype=torch.float64) for _ in range(4))
+    b, e = seq_shard(S, world, rank)
+    qs, ks, vs = (t[:, :, b:e].clone().requires_grad_(True) for t in (q, k, v))
+    o = seq_parallel_attention(qs, ks, vs, S, ops=OracleShardOps())
+    o.backward(do[:, :, b:e])
+    torch.save((o.detach(), qs.grad, ks.grad, vs.grad), os.path.join(out_dir, f"g{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,S", [(2, 3000), (3, 2600), (2, 1500)])
+def test_seq_parallel_backward_gloo(world, S, tmp_path):
+    """The sequence-split backward's exchanges -- dG summed over the ranks and
+    folded into each rank's own blocks, halo gradients sent back to the
+    previous rank -- give the whole sequence's gradients."""
+    from oracle import cra_oracle as O
+    mp.spawn(_bwd_worker, args=(world, _free_port(), S, str(tmp_path)), nprocs=world, join=True)
+    parts = [torch.load(tmp_path / f"g{r}.pt") for r in range(world)]
+    got = [torch.cat([p[i] for p in parts], dim=2) for i in range(4)]
+    g = torch.Generator().manual_seed(8)
+    q, k, v, do = (torch.randn(1, 2, S, 16, generator=g, dtype=torch.float64) for _ in range(4))
+    ref = O.forward_backward(q, k, v, do, dtype=torch.float64)
+    for x, y in zip(got, ref[:4]):
+        assert (x - y).abs().max().item() < 1e-9
