@@ -204,8 +204,9 @@ __global__ void __launch_bounds__(256) delta_kernel(const void* __restrict__ op,
 // stream, the S/dP -> softmax -> dQ pipeline and the epilogue all run across
 // tile boundaries, so no per-tile start-up or drain is exposed.
 //
-// Warps: 0 producer (TMA), 1 MMA issuer, 2-5 / 6-9 softmax (units of parity
-// 0 / 1), 10-13 epilogue.  TMEM lane = 32 * (warp % 4) + lane = query row.
+// Warps: 0 K / V producer (TMA), 1 MMA issuer, 2-5 / 6-9 softmax (units of
+// parity 0 / 1), 10-13 epilogue, 14 Q / dO producer.  TMEM lane = 32 * (warp
+// % 4) + lane = query row.
 // ===========================================================================
 // Optional cycle counters of the dQ pass (build with -DCRA_PROF; read with
 // cra_dq_prof): per role, cycles spent waiting on each barrier and working.
@@ -270,26 +271,27 @@ struct DqCfg {
   static constexpr int TB = kTile * D * 2;   // Q / dO tile
   static constexpr int UB = kUnit * D * 2;   // one K or V unit
   static constexpr int NSLOT = (D == 128) ? 10 : 20;  // ring entries K_0, V_0, K_1, V_1, ...
-  static constexpr int QPRE = 2;  // units of a new tile fetched before its Q / dO
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_DO = OFF_Q + TB;
   static constexpr int OFF_RING = OFF_DO + TB;
   static constexpr int OFF_BAR = OFF_RING + NSLOT * UB;
   static constexpr int B_QFULL = 0, B_QEMPTY = 1, B_FULL = 2, B_EMPTY = 2 + NSLOT, B_SFULL = 2 + 2 * NSLOT,
-                       B_DSFULL = B_SFULL + 2, B_ACCFULL = B_DSFULL + 2,
-                       B_ACCFREE = B_ACCFULL + 2, B_DRAIN = B_ACCFREE + 2, N_BAR = B_DRAIN + 1;
+                       B_DSFULL = B_SFULL + 2, B_ACCFULL = B_DSFULL + 2, B_ACCFREE = B_ACCFULL + 1,
+                       B_QREAD = B_ACCFREE + 1, B_DRAIN = B_QREAD + 1, N_BAR = B_DRAIN + 1;
   static constexpr int OFF_MISC = OFF_BAR + N_BAR * 8;
   static constexpr int SMEM = OFF_MISC + 16 + 1024;
   // TMEM: slot s -> S at 128 s, dP at 128 s + 64 (fp32, 64 columns each; dS
-  // overwrites the first 32 columns of S as 16-bit pairs); dQ accumulator a
-  // at 256 + 128 a
-  static constexpr int COL_DQ = 256;
-  static constexpr int THREADS = 448;
+  // overwrites the first 32 columns of S as 16-bit pairs); the tile's Q and
+  // dO as 16-bit pairs (the A operands of S and dP) at 256 and 256 + D / 2;
+  // the dQ accumulator after them
+  static constexpr int COL_Q = 256, COL_DO = COL_Q + D / 2, COL_DQ = 384;
+  static constexpr int THREADS = 480;
+  static constexpr int Q_WARP = 14;
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
 template <int D, bool BF16>
-__global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ QueryPassParams p) {
+__global__ void __launch_bounds__(480, 1) dq_kernel(const __grid_constant__ QueryPassParams p) {
   using C = DqCfg<D>;
   using E = Elt<BF16>;
   extern __shared__ uint8_t smem_raw[];
@@ -318,9 +320,10 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
     for (int s = 0; s < 2; ++s) {
       mbar_init(BAR(C::B_SFULL + s), 1);
       mbar_init(BAR(C::B_DSFULL + s), 128);
-      mbar_init(BAR(C::B_ACCFULL + s), 1);
-      mbar_init(BAR(C::B_ACCFREE + s), 128);
     }
+    mbar_init(BAR(C::B_ACCFULL), 1);
+    mbar_init(BAR(C::B_ACCFREE), 128);
+    mbar_init(BAR(C::B_QREAD), 1);
     mbar_init(BAR(C::B_DRAIN), 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -334,57 +337,17 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
   if (warp == 0) {
     // ---------------- producer ----------------
     if (lane == 0) {
-      int e = 0, nq = 0;  // ring entries issued, Q / dO tiles issued
+      int e = 0;  // ring entries issued
       bool ok = true;
       for (int t = blockIdx.x, it = 0; ok && t < n_tiles; t += gridDim.x, ++it) {
         const DqTile tl(t, p.n_qtiles, p.H, p.q_begin);
         const int hk = tl.h / p.kv_groups;
         const DqUnits un(tl.m0, q_end, W, R);
-        auto load_q = [&]() -> bool {
-          PROF_T(t0);
-          if (it > 0 && !mbar_wait(BAR(C::B_QEMPTY), (it - 1) & 1, ab)) return false;
-          PROF_ADD(0, t0);
-          mbar_expect_tx(BAR(C::B_QFULL), 2 * C::TB);
-          for (int c = 0; c < D / 64; ++c) {
-            tma_load_4d(sbase + C::OFF_Q + c * kTile * 128, &p.tm_q, BAR(C::B_QFULL), c * 64, tl.m0 - p.q_begin, tl.h, tl.b);
-            tma_load_4d(sbase + C::OFF_DO + c * kTile * 128, &p.tm_do, BAR(C::B_QFULL), c * 64, tl.m0 - p.q_begin, tl.h, tl.b);
-          }
-          ++nq;
-#ifndef CRA_DQ_NO_PREFETCH
-          // the next tile's Q / dO and first K / V units into L2: its Q / dO
-          // load can only start once this tile's last scores are issued
-          if (t + static_cast<int>(gridDim.x) < n_tiles) {
-            const DqTile tn(t + gridDim.x, p.n_qtiles, p.H, p.q_begin);
-            const DqUnits un2(tn.m0, q_end, W, R);
-            for (int c = 0; c < D / 64; ++c) {
-              tma_prefetch_l2_4d(&p.tm_q, c * 64, tn.m0 - p.q_begin, tn.h, tn.b);
-              tma_prefetch_l2_4d(&p.tm_do, c * 64, tn.m0 - p.q_begin, tn.h, tn.b);
-            }
-            int np = 0;
-            for (int j = 0; j < un2.ntiles && np < 4; ++j)
-              for (int hh = 0; hh < 2 && np < 4; ++hh) {
-                int row0;
-                bool g;
-                if (!un2.get(j, hh, row0, g) || (!g && p.has_edge && row0 < p.kv_begin)) continue;
-                ++np;
-                for (int c = 0; c < D / 64; ++c) {
-                  tma_prefetch_l2_4d(g ? &p.tm_gk : &p.tm_k, c * 64, g ? row0 : row0 - p.kv_begin, tn.h / p.kv_groups,
-                                     tn.b);
-                  tma_prefetch_l2_4d(g ? &p.tm_gv : &p.tm_v, c * 64, g ? row0 : row0 - p.kv_begin, tn.h / p.kv_groups,
-                                     tn.b);
-                }
-              }
-          }
-#endif
-          return true;
-        };
-        int lu = 0;  // units of this tile issued
         for (int j = 0; ok && j < un.ntiles; ++j)
           for (int hh = 0; hh < 2 && ok; ++hh) {
             int row0;
             bool g;
             if (!un.get(j, hh, row0, g)) continue;
-            if (lu++ == C::QPRE && !load_q()) { ok = false; break; }
             for (int kv = 0; kv < 2; ++kv, ++e) {
               const int sl = e % C::NSLOT;
               PROF_T(t0);
@@ -403,13 +366,43 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
                             g ? row0 : edge ? row0 - p.edge_begin : row0 - p.kv_begin, hk, tl.b);
             }
           }
-        if (ok && lu <= C::QPRE && !load_q()) ok = false;
       }
-      if (*abort_flag) {  // let copies in flight land before the CTA exits
+      if (*abort_flag)  // let copies in flight land before the CTA exits
         for (int i = (e > C::NSLOT ? e - C::NSLOT : 0); i < e; ++i)
           mbar_wait_bounded(BAR(C::B_FULL + i % C::NSLOT), (i / C::NSLOT) & 1);
-        if (nq > 0) mbar_wait_bounded(BAR(C::B_QFULL), (nq - 1) & 1);
+    }
+    __syncwarp();
+  } else if (warp == C::Q_WARP) {
+    // ---------------- Q / dO producer ----------------
+    // A thread of its own, so that the K / V stream runs on into the next
+    // tile while this one waits for the current tile's last scores (the
+    // single Q / dO buffer frees only then).
+    if (lane == 0) {
+      int nq = 0;
+      for (int t = blockIdx.x, it = 0; t < n_tiles; t += gridDim.x, ++it) {
+        const DqTile tl(t, p.n_qtiles, p.H, p.q_begin);
+        PROF_T(t0);
+        if (it > 0 && !mbar_wait(BAR(C::B_QEMPTY), (it - 1) & 1, ab)) break;
+        PROF_ADD(0, t0);
+        mbar_expect_tx(BAR(C::B_QFULL), 2 * C::TB);
+        for (int c = 0; c < D / 64; ++c) {
+          tma_load_4d(sbase + C::OFF_Q + c * kTile * 128, &p.tm_q, BAR(C::B_QFULL), c * 64, tl.m0 - p.q_begin, tl.h, tl.b);
+          tma_load_4d(sbase + C::OFF_DO + c * kTile * 128, &p.tm_do, BAR(C::B_QFULL), c * 64, tl.m0 - p.q_begin, tl.h, tl.b);
+        }
+        ++nq;
+#ifndef CRA_DQ_NO_PREFETCH
+        // the next tile's Q / dO into L2, so that its load, which waits for
+        // this tile's last scores, comes from L2
+        if (t + static_cast<int>(gridDim.x) < n_tiles) {
+          const DqTile tn(t + gridDim.x, p.n_qtiles, p.H, p.q_begin);
+          for (int c = 0; c < D / 64; ++c) {
+            tma_prefetch_l2_4d(&p.tm_q, c * 64, tn.m0 - p.q_begin, tn.h, tn.b);
+            tma_prefetch_l2_4d(&p.tm_do, c * 64, tn.m0 - p.q_begin, tn.h, tn.b);
+          }
+        }
+#endif
       }
+      if (*abort_flag && nq > 0) mbar_wait_bounded(BAR(C::B_QFULL), (nq - 1) & 1);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -424,21 +417,21 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
       bool ok = true;
       // dQ += dS K for unit i of tile iteration iti (its K sits in ring entry 2 i)
       auto issue_dq = [&](int i, int iti, bool first, bool last) -> bool {
-        const int sl = i & 1, ek = (2 * i) % C::NSLOT, acc = iti & 1;
+        const int sl = i & 1, ek = (2 * i) % C::NSLOT;
         PROF_T(t0);
         if (!warp_wait(BAR(C::B_DSFULL + sl), (i >> 1) & 1, ab)) return false;
         PROF_ADD(4, t0);
         PROF_T(t1);
-        if (first && iti >= 2 && !warp_wait(BAR(C::B_ACCFREE + acc), ((iti >> 1) - 1) & 1, ab)) return false;
+        if (first && iti >= 1 && !warp_wait(BAR(C::B_ACCFREE), (iti - 1) & 1, ab)) return false;
         PROF_ADD(5, t1);
         tc_fence_after();
         const uint64_t kd = sdesc(sbase + C::OFF_RING + ek * C::UB, kUnit * 128, 1024);
 #pragma unroll
         for (int kk = 0; kk < kUnit / 16; ++kk)
-          mma_ts_w(tmem + C::COL_DQ + 128 * acc, tmem + 128 * sl + kk * 8, kd + ((kk * 16 * 128) >> 4), ID_Q,
+          mma_ts_w(tmem + C::COL_DQ, tmem + 128 * sl + kk * 8, kd + ((kk * 16 * 128) >> 4), ID_Q,
                  (!first || kk > 0) ? 1u : 0u);
         mma_commit_w(BAR(C::B_EMPTY + ek));
-        if (last) mma_commit_w(BAR(C::B_ACCFULL + acc));
+        if (last) mma_commit_w(BAR(C::B_ACCFULL));
         return true;
       };
       PROF_T(tstart);
@@ -449,8 +442,24 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
         const DqTile tl(t, p.n_qtiles, p.H, p.q_begin);
         const DqUnits un(tl.m0, q_end, W, R);
         PROF_T(tq);
-        if (!warp_wait(BAR(C::B_QFULL), it & 1, ab)) { ok = false; break; }
+        // Q / dO into TMEM once the previous tile's last S / dP products
+        // (which read the TMEM copies) have completed; the copies execute in
+        // order before this tile's MMAs, and their commit frees the
+        // shared-memory buffer for the next tile's loads
+        if (!warp_wait(BAR(C::B_QFULL), it & 1, ab) ||
+            (it > 0 && !warp_wait(BAR(C::B_QREAD), (it - 1) & 1, ab))) {
+          ok = false;
+          break;
+        }
         PROF_ADD(6, tq);
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t qo = ((kk >> 2) * kTile * 128 + (kk & 3) * 32) >> 4;
+          tmem_cp_128x256b_w(tmem + C::COL_Q + kk * 8, qd + qo);
+          tmem_cp_128x256b_w(tmem + C::COL_DO + kk * 8, dd + qo);
+        }
+        mma_commit_w(BAR(C::B_QEMPTY));
         bool first = true;
         for (int j = 0; ok && j < un.ntiles; ++j)
           for (int hh = 0; ok && hh < 2; ++hh) {
@@ -476,10 +485,9 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
               // K-step kk: 64-column chunk kk / 4, 32-byte step kk % 4 in its 128-byte rows
-              const uint32_t qo = ((kk >> 2) * kTile * 128 + (kk & 3) * 32) >> 4;
               const uint32_t ko = ((kk >> 2) * kUnit * 128 + (kk & 3) * 32) >> 4;
-              mma_ss_w(tmem + 128 * sl, qd + qo, kd + ko, ID_S, kk > 0 ? 1u : 0u);
-              mma_ss_w(tmem + 128 * sl + 64, dd + qo, vd + ko, ID_S, kk > 0 ? 1u : 0u);
+              mma_ts_w(tmem + 128 * sl, tmem + C::COL_Q + kk * 8, kd + ko, ID_S, kk > 0 ? 1u : 0u);
+              mma_ts_w(tmem + 128 * sl + 64, tmem + C::COL_DO + kk * 8, vd + ko, ID_S, kk > 0 ? 1u : 0u);
             }
             mma_commit_w(BAR(C::B_SFULL + sl));
             mma_commit_w(BAR(C::B_EMPTY + ev % C::NSLOT));  // V_u is no longer needed
@@ -491,7 +499,7 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
             first = false;
             ++u;
           }
-        if (ok) mma_commit_w(BAR(C::B_QEMPTY));  // every S / dP of this tile issued
+        if (ok) mma_commit_w(BAR(C::B_QREAD));  // every S / dP of this tile issued
       }
       if (ok && u > 0) ok = issue_dq(u - 1, pit, pfirst, true);
       PROF_ADD(9, tstart);
@@ -580,28 +588,27 @@ __global__ void __launch_bounds__(448, 1) dq_kernel(const __grid_constant__ Quer
           PROF_ADD(13, t1);
         }
     }
-  } else {
+  } else if (warp < C::Q_WARP) {
     // ---------------- epilogue: dQ accumulator -> global ----------------
     const int r = ((warp & 3) << 5) | lane;
     const uint32_t lane_off = static_cast<uint32_t>(r & ~31) << 16;
     for (int t = blockIdx.x, it = 0; t < n_tiles; t += gridDim.x, ++it) {
       const DqTile tl(t, p.n_qtiles, p.H, p.q_begin);
-      const int acc = it & 1;
       PROF_T(t0);
-      if (!mbar_wait(BAR(C::B_ACCFULL + acc), (it >> 1) & 1, ab)) break;
+      if (!mbar_wait(BAR(C::B_ACCFULL), it & 1, ab)) break;
       PROF_ADD(16, t0);
       tc_fence_after();
       uint32_t pk[D / 2];
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         float o[32];
-        tmem_ld32(tmem + lane_off + C::COL_DQ + 128 * acc + 32 * c, o);
+        tmem_ld32(tmem + lane_off + C::COL_DQ + 32 * c, o);
         tmem_ld_wait();
 #pragma unroll
         for (int e2 = 0; e2 < 32; e2 += 2) pk[16 * c + e2 / 2] = E::pack(o[e2] * p.scale, o[e2 + 1] * p.scale);
       }
       tc_fence_before();
-      mbar_arrive(BAR(C::B_ACCFREE + acc));
+      mbar_arrive(BAR(C::B_ACCFREE));
       const int qi = tl.m0 + r;
       if (qi < q_end) {
         typename E::T* orow = reinterpret_cast<typename E::T*>(p.out) + tl.b * p.out_sb + tl.h * p.out_sh +

@@ -213,6 +213,16 @@ __device__ __forceinline__ void mma_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint6
       "r"(a_tmem), "l"(b), "r"(idesc), "r"(accum)
       : "memory");
 }
+// Copies a 128-row x 32-byte matrix (one K-step of 16 16-bit elements of a
+// K-major operand, described like an MMA operand) from shared memory to TMEM:
+// row i -> lane i, 8 consecutive columns, the layout a TS-form MMA reads its A
+// operand in.  Executes in order before later MMAs of the issuing thread.
+__device__ __forceinline__ void tmem_cp_128x256b_w(uint32_t taddr, uint64_t s) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.cp.cta_group::1.128x256b [%0], %1;\n\t}" ::"r"(taddr), "l"(s)
+      : "memory");
+}
 // Arrive on `bar` once every MMA the elected lane issued so far has completed
 // (a commit covers all earlier MMAs of the thread, not just the latest).
 __device__ __forceinline__ void mma_commit_w(uint32_t bar) {
