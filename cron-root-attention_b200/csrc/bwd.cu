@@ -196,11 +196,12 @@ __global__ void __launch_bounds__(256) delta_kernel(const void* __restrict__ op,
 // blockIdx.x, blockIdx.x + gridDim.x, ... (each a 128-query tile of one
 // (b, h), longest tiles first) and, per tile, the forward's key tiles (band,
 // then global prefix) in 64-key units, skipping halves no row needs.  Per
-// unit: S = Q K_u^T and dP = dO V_u^T into TMEM slot u & 1; softmax
-// warpgroup u & 1 writes dS = P * (dP - Di) (P from the stored lse, 16-bit)
-// back over S; dQ += dS K_u reads dS from TMEM (TS-form MMA) and accumulates
-// into one of two dQ accumulators (alternating tiles), which an epilogue
-// warpgroup drains to global memory while the next tile runs.  The K/V unit
+// unit: S = Q K_u^T and dP = dO V_u^T into TMEM slot u & 1 (TS-form MMAs:
+// the tile's Q and dO are copied into TMEM once per tile, so only K_u / V_u
+// are read from shared memory); softmax warpgroup u & 1 writes dS = P * (dP -
+// Di) (P from the stored lse, 16-bit) back over S; dQ += dS K_u reads dS from
+// TMEM (TS-form MMA) into the dQ accumulator, which an epilogue warpgroup
+// reads out while the next tile's first scores are computed.  The K/V unit
 // stream, the S/dP -> softmax -> dQ pipeline and the epilogue all run across
 // tile boundaries, so no per-tile start-up or drain is exposed.
 //
