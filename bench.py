@@ -223,7 +223,7 @@ TRAFFIC_H8 = {
     "keyglobal_kernel": 375.778048e6,
     "reduce_kernel": 123.899136e6,
     "keylocal_kernel": 788.465664e6,
-    "dq_kernel": 663.429632e6,
+    "dq_kernel": 660.156416e6,
     "dq_convert_kernel": None,
 }
 
