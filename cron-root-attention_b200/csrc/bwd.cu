@@ -698,16 +698,22 @@ __global__ void __launch_bounds__(320, 1) keyglobal_kernel(const __grid_constant
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int hk = blockIdx.y, b = blockIdx.z;
+  // CTAs in launch order take the global-row tiles first to last, all heads
+  // and splits of a tile together: earlier tiles are seen by more queries,
+  // so the longest CTAs start first and the last wave holds the shortest.
+  const int lin = static_cast<int>(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
+  const int per_tile = static_cast<int>(gridDim.y * gridDim.z) * p.n_split;
+  const int gt = lin / per_tile;
+  const int rem = lin % per_tile;
+  const int split = rem % p.n_split;
+  const int hk = (rem / p.n_split) % static_cast<int>(gridDim.y), b = (rem / p.n_split) / static_cast<int>(gridDim.y);
   const int W = p.W, S = p.S, R = p.R;
   const int q_lo = p.q_lo, q_hi = p.q_hi;
   const int n_units = (q_hi - q_lo + kUnit - 1) / kUnit;  // 64-query units from q_lo
   const int Spad = p.q_pad;
   const int groups = p.kv_groups;
 
-  // global-row tile and this split's 64-query units [t_lo, t_hi) (per group head)
-  const int gt = static_cast<int>(blockIdx.x) / p.n_split;
-  const int split = static_cast<int>(blockIdx.x) % p.n_split;
+  // global-row tile gt and this split's 64-query units [t_lo, t_hi) (per group head)
   const int k0 = gt * kTile;
   const int tmin = min(max(first_query_seeing(k0, S, W, R) - q_lo, 0) / kUnit, n_units);
   const int tot = n_units - tmin;
