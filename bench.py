@@ -220,8 +220,8 @@ TRAFFIC_H8 = {
     "fwd_kernel": 528.839680e6,
     "relay_build_kernel": 141.839616e6,
     "delta_kernel": 277.032192e6,
-    "keyglobal_kernel": 375.778048e6,
-    "reduce_kernel": 123.899136e6,
+    "keyglobal_kernel": 797.732864e6,
+    "reduce_kernel": 84.846848e6,
     "keylocal_kernel": 788.465664e6,
     "dq_kernel": 660.156416e6,
     "dq_convert_kernel": None,
