@@ -620,12 +620,85 @@ def strong_config(cfg: str, args, rank: int, world: int, local_rank: int) -> dic
     return out
 
 
+# Times the reference's own GPU path (cron_root_attention_v14 with its Triton
+# kernels, unmodified, from baseline/_ref) at the north-star shape on one GPU:
+# forward alone and forward + backward through its public API.  Runs in a
+# child process, since the reference's package has the same name as this
+# repository's.
+_REF_TRITON_CHILD = r"""
+import json, statistics, sys, time
+import torch
+ref = sys.argv[1]
+B, H, S, D, steps, warmup = (int(a) for a in sys.argv[2:8])
+sys.path.insert(0, ref)
+import cron_root_attention as R
+assert R.__file__.startswith(ref), R.__file__
+dev = torch.device("cuda", 0)
+g = torch.Generator(device=dev).manual_seed(2)
+q, k, v, do = (torch.randn(B, H, S, D, device=dev, generator=g).to(torch.bfloat16) for _ in range(4))
+def fwd():
+    with torch.no_grad():
+        return R.cron_root_attention(q, k, v)
+def step():
+    qq, kk, vv = (t.detach().requires_grad_(True) for t in (q, k, v))
+    R.cron_root_attention(qq, kk, vv).backward(do)
+def timed(fn):
+    t0 = time.time()
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    first_s = time.time() - t0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps, first_s
+fwd_ms, fwd_first = timed(fwd)
+step_ms, step_first = timed(step)
+print(json.dumps({"fwd_ms": fwd_ms, "fwdbwd_ms": step_ms, "warmup_s": [fwd_first, step_first]}))
+"""
+
+
+def run_reference_triton(args):
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    line = {"impl": "reference_triton", "metric": METRIC, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "config": {"workload": f"north star fwd and fwd+bwd, B{B} H{H} S{S} D{D} bf16", "B": B, "H": H, "S": S,
+                       "D": D, "data": "synthetic, seeded on the device (seed 2)"}}
+    if not os.path.isdir(os.path.join(ref, "cron_root_attention")):
+        line["unavailable"] = "baseline/_ref holds no install of the reference"
+        print(json.dumps(line), flush=True)
+        return
+    try:
+        r = subprocess.run([sys.executable, "-c", _REF_TRITON_CHILD, ref, str(B), str(H), str(S), str(D),
+                            str(args.steps), str(max(args.warmup, 3))],
+                           capture_output=True, text=True, timeout=1500)
+    except subprocess.TimeoutExpired:
+        line["unavailable"] = "the reference's Triton path did not finish in 1500 s"
+        print(json.dumps(line), flush=True)
+        return
+    out = [x for x in r.stdout.splitlines() if x.startswith("{")]
+    if r.returncode != 0 or not out:
+        line["unavailable"] = "the reference's Triton path failed: " + (r.stderr.strip().splitlines() or ["?"])[-1][:300]
+        print(json.dumps(line), flush=True)
+        return
+    res = json.loads(out[-1])
+    fwd_f, bwd_f = flops()
+    line.update({"fwd_ms": res["fwd_ms"], "fwd_tflops": fwd_f / (res["fwd_ms"] * 1e-3) / 1e12,
+                 "ms_per_step": res["fwdbwd_ms"], "value": (fwd_f + bwd_f) / (res["fwdbwd_ms"] * 1e-3) / 1e12,
+                 "unit": "TFLOP/s", "higher_is_better": True, "warmup_s": res["warmup_s"]})
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference_triton"],
+                    help="reference: the reference's CPU algorithm; reference_triton: the reference's own "
+                         "Triton GPU path, installed unmodified in baseline/_ref (rank 0, one GPU)")
     ap.add_argument("--mode", default="all", choices=["all", "fwd", "fwdbwd"],
                     help="fwd / fwdbwd: time only that pass (for profiling runs)")
     ap.add_argument("--no-strong", action="store_true", help="skip the config 4 / 5 strong-scaling legs")
@@ -644,6 +717,9 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
+        elif args.impl == "reference_triton":
+            if rank == 0:
+                run_reference_triton(args)
         else:
             run_ours(args, rank, world, local_rank)
     finally:
