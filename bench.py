@@ -657,6 +657,12 @@ def timed(fn):
     return e0.elapsed_time(e1) / steps, first_s
 fwd_ms, fwd_first = timed(fwd)
 step_ms, step_first = timed(step)
+if len(sys.argv) > 8:  # heads 0 and 1 of the output and the gradients, for the comparison
+    qq, kk, vv = (t.detach().requires_grad_(True) for t in (q, k, v))
+    o = R.cron_root_attention(qq, kk, vv)
+    o.backward(do)
+    torch.save({n: t[:, :2].detach().cpu() for n, t in (("o", o), ("dq", qq.grad), ("dk", kk.grad), ("dv", vv.grad))},
+               sys.argv[8])
 print(json.dumps({"fwd_ms": fwd_ms, "fwdbwd_ms": step_ms, "warmup_s": [fwd_first, step_first]}))
 """
 
@@ -670,9 +676,11 @@ def run_reference_triton(args):
         line["unavailable"] = "baseline/_ref holds no install of the reference"
         print(json.dumps(line), flush=True)
         return
+    import tempfile
+    dump = os.path.join(tempfile.mkdtemp(), "ref_out.pt")
     try:
         r = subprocess.run([sys.executable, "-c", _REF_TRITON_CHILD, ref, str(B), str(H), str(S), str(D),
-                            str(args.steps), str(max(args.warmup, 3))],
+                            str(args.steps), str(max(args.warmup, 3)), dump],
                            capture_output=True, text=True, timeout=1500)
     except subprocess.TimeoutExpired:
         line["unavailable"] = "the reference's Triton path did not finish in 1500 s"
@@ -688,6 +696,22 @@ def run_reference_triton(args):
     line.update({"fwd_ms": res["fwd_ms"], "fwd_tflops": fwd_f / (res["fwd_ms"] * 1e-3) / 1e12,
                  "ms_per_step": res["fwdbwd_ms"], "value": (fwd_f + bwd_f) / (res["fwdbwd_ms"] * 1e-3) / 1e12,
                  "unit": "TFLOP/s", "higher_is_better": True, "warmup_s": res["warmup_s"]})
+    # this library on the same inputs: heads 0 and 1 of o, dq, dk, dv against the reference's
+    if os.path.exists(dump):
+        import cron_root_attention as cra
+        refo = torch.load(dump)
+        dev = torch.device("cuda", 0)
+        g = torch.Generator(device=dev).manual_seed(2)
+        q, k, v, do = (torch.randn(B, H, S, D, device=dev, generator=g).to(torch.bfloat16) for _ in range(4))
+        qq, kk, vv = (t.detach().requires_grad_(True) for t in (q, k, v))
+        o = cra.cron_root_attention(qq, kk, vv)
+        o.backward(do)
+        cmp = {}
+        for n, t in (("o", o), ("dq", qq.grad), ("dk", kk.grad), ("dv", vv.grad)):
+            a, b = t[:, :2].detach().float().cpu(), refo[n].float()
+            cmp[n] = {"max_abs": (a - b).abs().max().item(), "mean_abs": (a - b).abs().mean().item(),
+                      "rel_l2": ((a - b).norm() / b.norm()).item()}
+        line["vs_reference_gpu_heads01"] = cmp
     print(json.dumps(line), flush=True)
 
 
