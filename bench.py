@@ -663,7 +663,14 @@ if len(sys.argv) > 8:  # heads 0 and 1 of the output and the gradients, for the 
     o.backward(do)
     torch.save({n: t[:, :2].detach().cpu() for n, t in (("o", o), ("dq", qq.grad), ("dk", kk.grad), ("dv", vv.grad))},
                sys.argv[8])
-print(json.dumps({"fwd_ms": fwd_ms, "fwdbwd_ms": step_ms, "warmup_s": [fwd_first, step_first]}))
+# forward alone at BASELINE configs 2 and 4 (one GPU)
+fwd_cfg = {}
+for name, (b_, h_, s_, d_, sd, sig) in {"c2": (1, 12, 16384, 64, 1, 0.5), "c4": (1, 32, 262144, 128, 3, 0.5)}.items():
+    g = torch.Generator(device=dev).manual_seed(sd)
+    q, k, v = ((torch.randn(b_, h_, s_, d_, device=dev, generator=g) * sig).to(torch.float16) for _ in range(3))
+    fwd_cfg[name] = timed(fwd)[0]
+    del q, k, v
+print(json.dumps({"fwd_ms": fwd_ms, "fwdbwd_ms": step_ms, "warmup_s": [fwd_first, step_first], "fwd_cfg": fwd_cfg}))
 """
 
 
@@ -712,6 +719,31 @@ def run_reference_triton(args):
             cmp[n] = {"max_abs": (a - b).abs().max().item(), "mean_abs": (a - b).abs().mean().item(),
                       "rel_l2": ((a - b).norm() / b.norm()).item()}
         line["vs_reference_gpu_heads01"] = cmp
+        # forward at configs 2 and 4, this library beside the reference, same inputs
+        other = {}
+        for name, (b_, h_, s_, d_, sd, sig) in {"c2": (1, 12, 16384, 64, 1, 0.5),
+                                               "c4": (1, 32, 262144, 128, 3, 0.5)}.items():
+            g = torch.Generator(device=dev).manual_seed(sd)
+            q, k, v = ((torch.randn(b_, h_, s_, d_, device=dev, generator=g) * sig).to(torch.float16)
+                       for _ in range(3))
+            with torch.no_grad():
+                for _ in range(3):
+                    cra.cron_root_attention(q, k, v)
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(args.steps):
+                    cra.cron_root_attention(q, k, v)
+                e1.record()
+                torch.cuda.synchronize()
+                ms = e0.elapsed_time(e1) / args.steps
+            f = 4.0 * d_ * visible_pairs(s_) * b_ * h_
+            rms = res.get("fwd_cfg", {}).get(name)
+            other[name] = {"shape": f"B{b_} H{h_} S{s_} D{d_} fp16", "ours_fwd_ms": ms,
+                           "ours_fwd_tflops": f / (ms * 1e-3) / 1e12, "reference_fwd_ms": rms,
+                           "reference_fwd_tflops": f / (rms * 1e-3) / 1e12 if rms else None}
+            del q, k, v
+        line["fwd_configs"] = other
     print(json.dumps(line), flush=True)
 
 
